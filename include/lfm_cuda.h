@@ -1,0 +1,189 @@
+/*
+ * lfm_cuda.h — C ABI of the B200 (sm_100a) LFM2.5-8B-A1B Q6_K token-loop engine.
+ *
+ * This is the drop-in boundary that replaces the reference's
+ * `lfm2_engine::gpu_lfm::GpuEngine` (engine/src/gpu_lfm.rs:23-245 and
+ * engine/src/gpu_lfm/resident_graph.rs:90-602) for its callers
+ * (`lfm2-greedy`, engine/src/main.rs:196-281; `api_stream`,
+ * engine/src/bin/api_stream.rs:47-77; `persistent`). Each entry point cites
+ * the reference method it stands in for.
+ *
+ * Conventions
+ *  - Plain C types only; no CUDA or torch types cross the boundary.
+ *  - Every call returns an lfm_status; on failure lfm_last_error() (engine
+ *    calls) or lfm_global_error() (creation) holds a message. No C++
+ *    exception crosses the boundary.
+ *  - Calls are synchronous and blocking: they return after the device work
+ *    they issued has completed, like the reference's fence-waited submits
+ *    (engine/src/vulkan.rs:435-545). One engine per GPU per host thread; an
+ *    engine is not thread-safe (the reference's GpuOps is !Sync).
+ *  - The engine owns all device memory; callers own host buffers.
+ *  - Input validation follows the reference: ids < vocab, n >= 1,
+ *    start_pos + n <= ctx, ctx <= 4096 (resident_graph.rs:161-172,
+ *    ops.rs:488-491), 1..=64 ids for lfm_forward_token
+ *    (resident_graph.rs:95-98).
+ */
+#ifndef LFM_CUDA_H
+#define LFM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t lfm_status;
+#define LFM_OK 0
+#define LFM_ERR_ARG 1        /* invalid argument (range, size, null) */
+#define LFM_ERR_MODEL 2      /* GGUF parse / geometry / missing tensor */
+#define LFM_ERR_CUDA 3       /* CUDA runtime error */
+#define LFM_ERR_STATE 4      /* call not valid in the current engine state */
+#define LFM_ERR_DEVICE 5     /* device-side status word reported a failure */
+
+#define LFM_MAX_CTX 4096u
+#define LFM_PREFILL_CHUNK 64u /* work_bound.rs:6 PREFILL_CHUNK */
+
+typedef struct lfm_engine lfm_engine;
+
+/* Hyperparams (engine/src/lfm.rs:31-49, load_hyperparams :102-145). */
+typedef struct lfm_hparams {
+  uint32_t dim, heads, head_dim, n_layers, vocab;
+  uint32_t n_expert, n_used, expert_ff, n_ff, dense_lead, conv_l_cache;
+  uint32_t eos;
+  float eps, rope_theta;
+  uint32_t kv_heads[64]; /* per layer: 0 = short-conv, 8 = attention */
+} lfm_hparams;
+
+/* Counters reported by the reference's result lines (main.rs:273-280,
+ * persistent.rs:230-242): dispatches, GPU argmax, decode-plan reuse. */
+typedef struct lfm_counters {
+  uint64_t kernel_launches;       /* gpu_dispatch_count */
+  uint64_t gpu_argmax;            /* gpu_argmax_dispatches */
+  uint64_t graph_replays;         /* decode_command_buffer_reuses */
+  uint64_t graph_captures;
+  uint64_t prefill_tokens;        /* prefill_weight_reuse_tokens */
+  uint64_t expert_grouped_launches; /* expert_grouped_dispatches */
+} lfm_counters;
+
+/* ---- engine lifetime ------------------------------------------------- */
+
+/* GpuEngine::load(&ModelFile) (gpu_lfm.rs:51-115): parse the GGUF, validate
+ * geometry (lfm.rs:115-126), repack every Q6_K tensor into the device layout
+ * and upload it. `device` is the CUDA ordinal. */
+lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out);
+void lfm_engine_destroy(lfm_engine* e);
+
+/* GpuEngine::set_ctx (gpu_lfm.rs:117-119). ctx <= 4096. Takes effect before
+ * the first forward (resident state is sized on first use, like
+ * resident_graph.rs:173-181). */
+lfm_status lfm_engine_set_ctx(lfm_engine* e, uint32_t ctx);
+
+/* GpuEngine.hp (lfm.rs:31-49). */
+lfm_status lfm_hparams_get(lfm_engine* e, lfm_hparams* out);
+
+/* ---- token loop ------------------------------------------------------ */
+
+/* GpuEngine::forward(ids, start_pos) -> Vec<f32> (gpu_lfm.rs:243-245 ->
+ * resident_graph.rs:160-557): run n tokens starting at start_pos, write the
+ * last token's full-vocabulary logits (vocab floats) into `logits`. */
+lfm_status lfm_forward_logits(lfm_engine* e, const uint32_t* ids, uint32_t n,
+                              int64_t start_pos, float* logits);
+
+/* GpuEngine::forward_token(ids, position) -> u32 (resident_graph.rs:90-101):
+ * 1..=64 ids, device-side argmax of the last token's logits (ties -> lowest
+ * id, NaN never wins; kernels/persistent.rs:12-53). n == 1 replays the
+ * resident CUDA graph of the decode step. */
+lfm_status lfm_forward_token(lfm_engine* e, const uint32_t* ids, uint32_t n,
+                             uint32_t position, uint32_t* next_token);
+
+/* Device-resident greedy loop (main.rs:174-195 / api_stream.rs:56-77 with the
+ * host only reading results): prefill `prompt` in <=64-token chunks, then
+ * decode up to n tokens, stopping at `eos`. Tokens go to out_tokens (cap n);
+ * *n_out receives the count. Equivalent to calling lfm_forward_token in a
+ * loop (the api_stream request loop). */
+lfm_status lfm_generate(lfm_engine* e, const uint32_t* prompt, uint32_t prompt_len,
+                        uint32_t n, uint32_t eos, uint32_t* out_tokens, uint32_t* n_out);
+
+/* Device-resident greedy decode: `steps` decode steps starting with
+ * first_token at start_pos, each step consuming the previous step's device
+ * argmax with no host round trip (the reference's replayed decode plan with a
+ * device-side position, vulkan/reusable.rs:135-173, without its per-step
+ * fence wait). out_tokens receives every step's argmax (no EOS stop);
+ * *device_ms the CUDA-event time of steps 2..steps (of step 1 if steps == 1). */
+lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_pos, uint32_t steps,
+                           uint32_t* out_tokens, float* device_ms);
+
+/* CUDA-event device time (ms) of the last forward / decode call. */
+float lfm_last_device_ms(lfm_engine* e);
+
+/* GpuEngine::reset_session (resident_graph.rs:105-115): zero the short-conv
+ * state; stale KV beyond the valid prefix is never attended. */
+lfm_status lfm_reset_session(lfm_engine* e);
+
+/* GpuEngine::snapshot_resident_cache(valid) (resident_graph.rs:572-602):
+ * per layer in order, attention layers write K then V for positions
+ * [0,valid) as f32 words laid out [p][kv_head*64+d]; short-conv layers write
+ * their state as [channel][slot] f32. Pass buf = NULL to query *len. */
+lfm_status lfm_snapshot_cache(lfm_engine* e, uint32_t valid, uint8_t* buf, size_t cap,
+                              size_t* len);
+
+/* GpuEngine::restore_session(valid, bytes) (resident_graph.rs:119-158): the
+ * inverse of lfm_snapshot_cache; K/V words are rounded to fp16 storage. */
+lfm_status lfm_restore_cache(lfm_engine* e, uint32_t valid, const uint8_t* buf, size_t len);
+
+/* GpuEngine::snapshot_resident_logits (resident_graph.rs:561-568): the last
+ * full-vocabulary logits left on the device (vocab floats). */
+lfm_status lfm_snapshot_logits(lfm_engine* e, float* logits);
+
+lfm_status lfm_counters_get(lfm_engine* e, lfm_counters* out);
+const char* lfm_device_name(lfm_engine* e);      /* GpuEngine::device_name */
+const char* lfm_last_error(lfm_engine* e);
+const char* lfm_global_error(void);              /* failures before an engine exists */
+
+/* ---- kernel-level entry points (device pointers, for parity tests and
+ * the Q6_K microbench; stream = cudaStream_t or NULL) ------------------- */
+
+/* Size in bytes of the device layout of a [in_dim, rows] Q6_K matrix (equal
+ * to the GGUF size: every byte kept, no padding). */
+size_t lfm_q6k_device_bytes(uint32_t in_dim, uint32_t rows);
+
+/* Repack GGUF Q6_K rows (210-byte super-blocks, q6k.rs:8-17) held in HOST
+ * memory into the device layout at `dst_dev` (the reference's load-time
+ * repack, q6k.rs:25-39 / gpu_lfm.rs:83-87). */
+lfm_status lfm_q6k_upload(const uint8_t* gguf_rows, uint32_t in_dim, uint32_t rows, void* dst_dev);
+
+/* Dequantise rows [row0, row0+nrows) of a device-layout matrix to f32
+ * (bit-exact with q6k.rs:74-146). out_dev: nrows*in_dim floats. */
+lfm_status lfm_q6k_dequant(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t row0,
+                           uint32_t nrows, float* out_dev, void* stream);
+
+/* y[o + j*rows] = sum_k W[o,k] x[k + j*in_dim] for n columns (q6k_matmul,
+ * ops.rs:340-374). */
+lfm_status lfm_q6k_matmul(const void* w_dev, uint32_t in_dim, uint32_t rows, const float* x_dev,
+                          uint32_t n, float* y_dev, void* stream);
+
+/* Routed-expert matvec (q6k_routed, resident_graph.rs:446-495): for slot
+ * s < 4, y[s*rows + o] = sum_k W[expert_ids[s]][o,k] x[s*x_stride + k].
+ * `w_dev` holds all experts ([in_dim, rows, n_expert]); expert_ids_dev is a
+ * device int32[4]. */
+lfm_status lfm_q6k_routed(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t n_expert,
+                          const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_stride,
+                          float* y_dev, void* stream);
+
+/* Sigmoid router + top-k (kernels/resident.rs:58-99, lfm.rs:613-637) for n
+ * tokens: logits [n][n_expert] -> sel_ids [n][4] int32, sel_w [n][4] f32. */
+lfm_status lfm_route(const float* logits_dev, const float* bias_dev, uint32_t n_expert, uint32_t n,
+                     int32_t* sel_ids_dev, float* sel_w_dev, void* stream);
+
+/* Deterministic argmax (kernels/persistent.rs:12-53): first maximum, NaN
+ * never wins. */
+lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream);
+
+/* Message of the last failing kernel-level call on this thread. */
+const char* lfm_ops_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LFM_CUDA_H */

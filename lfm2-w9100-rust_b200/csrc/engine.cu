@@ -1,0 +1,979 @@
+// The B200 engine behind include/lfm_cuda.h — the replacement of the
+// reference's GpuEngine (engine/src/gpu_lfm.rs:23-245) and its resident graph
+// (engine/src/gpu_lfm/resident_graph.rs:4-602).
+//
+// Device data layout (HBM):
+//   * every Q6_K tensor in the unit-plane layout of q6k.cuh (same byte count
+//     as the GGUF payload); experts [in, out, 32] are one matrix of 32*out rows;
+//   * F32 tensors (norms, router, bias, conv taps) as in the GGUF;
+//   * K and V caches fp16 [attn layer][kv head][ctx][64] (the reference rounds
+//     K/V through f16, gpu_lfm.rs:8-11, so fp16 storage holds the same values);
+//   * short-conv state f32 [conv layer][channel][2] (resident_graph.rs:75);
+//   * RoPE (cos, sin) table [ctx][32] computed once on the host with the same
+//     libm calls and operation order as the CPU path (lfm.rs:248-267).
+// A decode step (n == 1) is one CUDA graph: a 8-byte H2D copy of (token,
+// position), ~130 kernels chained with programmatic dependent launch, and a
+// 4-byte D2H copy of the argmax — the analogue of the reference's immutable
+// decode replay with a device-side position (vulkan/reusable.rs:4-173).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <stdexcept>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/lfm_cuda.h"
+#include "gguf.h"
+#include "kernels.h"
+
+namespace lfm {
+
+void gemm_q6_ld(const Q6Mat& W, const float* X, int n, float* out, int ldo, bool resid, cudaStream_t s);
+
+namespace {
+
+thread_local std::string g_error;
+
+struct LayerW {
+  bool attn = false;
+  int attn_idx = -1, conv_idx = -1, moe_idx = -1;
+  const float *attn_norm = nullptr, *ffn_norm = nullptr;
+  Q6Mat q{}, k{}, v{}, o{};
+  const float *q_norm = nullptr, *k_norm = nullptr;
+  Q6Mat in_proj{}, out_proj{};
+  const float* conv_w = nullptr;
+  bool dense = false;
+  Q6Mat gate{}, up{}, down{};
+  const float *router = nullptr, *bias = nullptr;
+  Q6Mat gate_x{}, up_x{}, down_x{};
+};
+
+struct CudaError {
+  cudaError_t e;
+};
+
+#define CK(call)                                  \
+  do {                                            \
+    cudaError_t _e = (call);                      \
+    if (_e != cudaSuccess) throw ::lfm::CudaError{_e}; \
+  } while (0)
+
+}  // namespace
+
+struct EngineImpl {
+  int device = 0;
+  int sms = 148;
+  std::string name;
+  cudaStream_t stream = nullptr;
+  lfm_hparams hp{};
+  std::vector<LayerW> layers;
+  Q6Mat embd{};
+  const float* out_norm = nullptr;
+  std::vector<void*> weight_allocs;
+  size_t weight_bytes = 0;
+  int n_attn = 0, n_conv = 0, n_moe = 0;
+  bool pdl = true;
+  bool use_graph = true;
+
+  // resident state
+  uint32_t ctx = 4096;
+  bool state_ready = false;
+  uint32_t state_ctx = 0;
+  __half *kc = nullptr, *vc = nullptr;
+  float* conv_state = nullptr;
+  float2* rope = nullptr;
+  // decode buffers
+  float *x = nullptr, *qkv = nullptr, *a = nullptr, *gated = nullptr, *sw = nullptr, *down = nullptr,
+        *logits = nullptr, *attn_part = nullptr, *selw = nullptr;
+  int* sel = nullptr;
+  int* io = nullptr;  // [0] token, [1] position, [2] next token
+  unsigned* counters = nullptr;
+  float2* am_part = nullptr;
+  int* h_io = nullptr;  // pinned
+  // prefill buffers (capacity ncap tokens)
+  int ncap = 0;
+  float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pa = nullptr, *pbcx = nullptr, *pgated = nullptr,
+        *pgate = nullptr, *pup = nullptr, *psw = nullptr, *pdown = nullptr, *prlog = nullptr, *pselw = nullptr;
+  int *psel = nullptr, *pgroups = nullptr;
+  uint32_t* pids = nullptr;
+  std::vector<void*> state_allocs, prefill_allocs;
+
+  cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t loop_graph = nullptr;  // advance + decode step, token fed back on device
+  uint32_t* loop_tokens = nullptr;       // device record of loop tokens
+  uint32_t loop_cap = 0;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  lfm_counters ctr{};
+  std::string err;
+  int launches_per_decode = 0;
+
+  ~EngineImpl() {
+    cudaSetDevice(device);
+    if (graph) cudaGraphExecDestroy(graph);
+    if (loop_graph) cudaGraphExecDestroy(loop_graph);
+    if (loop_tokens) cudaFree(loop_tokens);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    free_prefill();
+    free_state();
+    for (void* p : weight_allocs) cudaFree(p);
+    if (h_io) cudaFreeHost(h_io);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  template <class T>
+  T* dalloc(std::vector<void*>& list, size_t count) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 16)));
+    list.push_back(p);
+    return (T*)p;
+  }
+  void free_state() {
+    for (void* p : state_allocs) cudaFree(p);
+    state_allocs.clear();
+    state_ready = false;
+    if (graph) {
+      cudaGraphExecDestroy(graph);
+      graph = nullptr;
+    }
+    if (loop_graph) {
+      cudaGraphExecDestroy(loop_graph);
+      loop_graph = nullptr;
+    }
+  }
+  void free_prefill() {
+    for (void* p : prefill_allocs) cudaFree(p);
+    prefill_allocs.clear();
+    ncap = 0;
+  }
+
+  // ------------------------------------------------------------- loading
+  bool load(const char* path);
+  void upload_q6(const GgufFile& f, const GgufTensor& t, int rows, int nb, Q6Mat& out,
+                 std::vector<uint8_t>& src, std::vector<uint8_t>& dst);
+  const float* upload_f32(const GgufFile& f, const GgufTensor& t);
+
+  // --------------------------------------------------------------- state
+  void ensure_state();
+  void ensure_prefill(int n);
+
+  // ------------------------------------------------------------- forward
+  void enqueue_decode(cudaStream_t s, bool pdl_on);
+  void run_decode(uint32_t token, uint32_t pos);
+  void run_prefill(const uint32_t* ids, int n, uint32_t start);
+  void run_loop(uint32_t steps, uint32_t* out_tokens);
+  std::vector<uint8_t> snapshot(uint32_t valid);
+  void restore(uint32_t valid, const uint8_t* buf, size_t len);
+};
+
+namespace {
+
+void set_err(EngineImpl* e, const std::string& m) {
+  if (e) e->err = m;
+  g_error = m;
+}
+
+}  // namespace
+
+void EngineImpl::upload_q6(const GgufFile& f, const GgufTensor& t, int rows, int nb, Q6Mat& out,
+                           std::vector<uint8_t>& src, std::vector<uint8_t>& dst) {
+  const size_t bytes = q6_total_bytes(rows, nb);
+  if (t.nbytes != bytes) throw std::runtime_error("tensor " + t.name + " has unexpected size");
+  src.resize(bytes);
+  dst.resize(bytes);
+  if (!f.read(t, 0, bytes, src.data())) throw std::runtime_error("read tensor " + t.name);
+  const int nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> th;
+  const size_t per = (rows + nthreads - 1) / nthreads;
+  for (int i = 0; i < nthreads; i++) {
+    const size_t r0 = i * per;
+    if (r0 >= (size_t)rows) break;
+    const size_t r1 = std::min<size_t>(rows, r0 + per);
+    th.emplace_back([&, r0, r1] {
+      q6_repack_rows(src.data() + r0 * nb * QB, r0, r1 - r0, nb, rows, dst.data());
+    });
+  }
+  for (auto& x : th) x.join();
+  void* d = nullptr;
+  CK(cudaMalloc(&d, bytes));
+  weight_allocs.push_back(d);
+  CK(cudaMemcpy(d, dst.data(), bytes, cudaMemcpyHostToDevice));
+  weight_bytes += bytes;
+  out = q6_view(d, rows, nb);
+}
+
+const float* EngineImpl::upload_f32(const GgufFile& f, const GgufTensor& t) {
+  std::vector<uint8_t> buf(t.nbytes);
+  if (!f.read(t, 0, t.nbytes, buf.data())) throw std::runtime_error("read tensor " + t.name);
+  void* d = nullptr;
+  CK(cudaMalloc(&d, t.nbytes));
+  weight_allocs.push_back(d);
+  CK(cudaMemcpy(d, buf.data(), t.nbytes, cudaMemcpyHostToDevice));
+  weight_bytes += t.nbytes;
+  return (const float*)d;
+}
+
+bool EngineImpl::load(const char* path) {
+  GgufFile f;
+  if (!f.open(path)) {
+    set_err(this, "parse GGUF header: " + f.err());
+    return false;
+  }
+  // load_hyperparams (lfm.rs:102-145)
+  uint32_t nl, dim, heads, vocab, ne, nu, eff, nff;
+  std::vector<uint32_t> kvh;
+  const char* keys[] = {"lfm2moe.block_count", "lfm2moe.embedding_length", "lfm2moe.attention.head_count",
+                        "lfm2moe.vocab_size", "lfm2moe.expert_count", "lfm2moe.expert_used_count",
+                        "lfm2moe.expert_feed_forward_length", "lfm2moe.feed_forward_length"};
+  uint32_t* outs[] = {&nl, &dim, &heads, &vocab, &ne, &nu, &eff, &nff};
+  for (int i = 0; i < 8; i++)
+    if (!f.meta_u32(keys[i], *outs[i])) {
+      set_err(this, std::string("metadata ") + keys[i] + " not a u32");
+      return false;
+    }
+  if (!f.meta_u32_array("lfm2moe.attention.head_count_kv", kvh)) {
+    set_err(this, "metadata lfm2moe.attention.head_count_kv not an array");
+    return false;
+  }
+  if (dim != DIM || heads != HEADS || nl != 24 || vocab != 128000 || ne != N_EXPERT || nu != N_USED ||
+      eff != EXPERT_FF) {
+    char b[256];
+    snprintf(b, sizeof b,
+             "unsupported geometry: dim=%u heads=%u layers=%u vocab=%u n_expert=%u n_used=%u expert_ff=%u", dim,
+             heads, nl, vocab, ne, nu, eff);
+    set_err(this, b);
+    return false;
+  }
+  if (kvh.size() != nl) {
+    set_err(this, "head_count_kv length differs from block_count");
+    return false;
+  }
+  hp.dim = dim;
+  hp.heads = heads;
+  hp.head_dim = HEAD_DIM;
+  hp.n_layers = nl;
+  hp.vocab = vocab;
+  hp.n_expert = ne;
+  hp.n_used = nu;
+  hp.expert_ff = eff;
+  hp.n_ff = nff;
+  hp.dense_lead = f.meta_u32_default("lfm2moe.leading_dense_block_count", 2);
+  hp.conv_l_cache = f.meta_u32_default("lfm2moe.shortconv.l_cache", 3);
+  hp.eos = f.meta_u32_default("tokenizer.ggml.eos_token_id", 124900);
+  if (!f.meta_f32("lfm2moe.attention.layer_norm_rms_epsilon", hp.eps) ||
+      !f.meta_f32("lfm2moe.rope.freq_base", hp.rope_theta)) {
+    set_err(this, "metadata eps / rope.freq_base not an f32");
+    return false;
+  }
+  for (uint32_t l = 0; l < nl; l++) hp.kv_heads[l] = kvh[l];
+  if (hp.conv_l_cache != 3 || nff != N_FF || hp.dense_lead > nl) {
+    set_err(this, "unsupported short-conv / dense FFN geometry");
+    return false;
+  }
+  for (uint32_t l = 0; l < nl; l++)
+    if (kvh[l] != 0 && kvh[l] != KV_HEADS) {
+      set_err(this, "attention layers must have 8 KV heads");
+      return false;
+    }
+
+  auto need = [&](const std::string& name, uint32_t type, std::vector<uint64_t> ne_) -> const GgufTensor& {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) throw std::runtime_error("missing tensor " + name);
+    if (t->type != type || t->ne != ne_) throw std::runtime_error("tensor " + name + " has unexpected type/shape");
+    return *t;
+  };
+  std::vector<uint8_t> src, dst;
+  try {
+    CK(cudaSetDevice(device));
+    const GgufTensor& te = need("token_embd.weight", 14, {DIM, vocab});
+    upload_q6(f, te, vocab, DIM / QK, embd, src, dst);
+    out_norm = upload_f32(f, need("token_embd_norm.weight", 0, {DIM}));
+    layers.resize(nl);
+    for (uint32_t l = 0; l < nl; l++) {
+      LayerW& L = layers[l];
+      const std::string p = "blk." + std::to_string(l) + ".";
+      L.attn_norm = upload_f32(f, need(p + "attn_norm.weight", 0, {DIM}));
+      L.ffn_norm = upload_f32(f, need(p + "ffn_norm.weight", 0, {DIM}));
+      if (kvh[l] > 0) {
+        L.attn = true;
+        L.attn_idx = n_attn++;
+        upload_q6(f, need(p + "attn_q.weight", 14, {DIM, DIM}), DIM, DIM / QK, L.q, src, dst);
+        upload_q6(f, need(p + "attn_k.weight", 14, {DIM, 512}), 512, DIM / QK, L.k, src, dst);
+        upload_q6(f, need(p + "attn_v.weight", 14, {DIM, 512}), 512, DIM / QK, L.v, src, dst);
+        upload_q6(f, need(p + "attn_output.weight", 14, {DIM, DIM}), DIM, DIM / QK, L.o, src, dst);
+        L.q_norm = upload_f32(f, need(p + "attn_q_norm.weight", 0, {HEAD_DIM}));
+        L.k_norm = upload_f32(f, need(p + "attn_k_norm.weight", 0, {HEAD_DIM}));
+      } else {
+        L.conv_idx = n_conv++;
+        upload_q6(f, need(p + "shortconv.in_proj.weight", 14, {DIM, 3 * DIM}), 3 * DIM, DIM / QK, L.in_proj, src,
+                  dst);
+        upload_q6(f, need(p + "shortconv.out_proj.weight", 14, {DIM, DIM}), DIM, DIM / QK, L.out_proj, src, dst);
+        L.conv_w = upload_f32(f, need(p + "shortconv.conv.weight", 0, {3, DIM}));
+      }
+      if (l < hp.dense_lead) {
+        L.dense = true;
+        upload_q6(f, need(p + "ffn_gate.weight", 14, {DIM, N_FF}), N_FF, DIM / QK, L.gate, src, dst);
+        upload_q6(f, need(p + "ffn_up.weight", 14, {DIM, N_FF}), N_FF, DIM / QK, L.up, src, dst);
+        upload_q6(f, need(p + "ffn_down.weight", 14, {N_FF, DIM}), DIM, N_FF / QK, L.down, src, dst);
+      } else {
+        L.moe_idx = n_moe++;
+        L.router = upload_f32(f, need(p + "ffn_gate_inp.weight", 0, {DIM, N_EXPERT}));
+        L.bias = upload_f32(f, need(p + "exp_probs_b.bias", 0, {N_EXPERT}));
+        upload_q6(f, need(p + "ffn_gate_exps.weight", 14, {DIM, EXPERT_FF, N_EXPERT}), N_EXPERT * EXPERT_FF,
+                  DIM / QK, L.gate_x, src, dst);
+        upload_q6(f, need(p + "ffn_up_exps.weight", 14, {DIM, EXPERT_FF, N_EXPERT}), N_EXPERT * EXPERT_FF,
+                  DIM / QK, L.up_x, src, dst);
+        upload_q6(f, need(p + "ffn_down_exps.weight", 14, {EXPERT_FF, DIM, N_EXPERT}), N_EXPERT * DIM,
+                  EXPERT_FF / QK, L.down_x, src, dst);
+      }
+    }
+  } catch (const std::exception& ex) {
+    set_err(this, ex.what());
+    return false;
+  } catch (const CudaError& ce) {
+    set_err(this, std::string("CUDA: ") + cudaGetErrorString(ce.e));
+    return false;
+  }
+  return true;
+}
+
+void EngineImpl::ensure_state() {
+  if (state_ready && state_ctx == ctx) return;
+  free_state();
+  const size_t kvsz = (size_t)std::max(n_attn, 1) * KV_HEADS * ctx * HEAD_DIM;
+  kc = dalloc<__half>(state_allocs, kvsz);
+  vc = dalloc<__half>(state_allocs, kvsz);
+  CK(cudaMemsetAsync(kc, 0, kvsz * 2, stream));
+  CK(cudaMemsetAsync(vc, 0, kvsz * 2, stream));
+  conv_state = dalloc<float>(state_allocs, (size_t)std::max(n_conv, 1) * DIM * 2);
+  CK(cudaMemsetAsync(conv_state, 0, (size_t)std::max(n_conv, 1) * DIM * 2 * 4, stream));
+  // RoPE table: theta = pos * tscale^p, tscale = theta_base^(-2/64) (lfm.rs:251-256).
+  {
+    std::vector<float2> t((size_t)ctx * 32);
+    float (*volatile p_powf)(float, float) = powf;
+    float (*volatile p_sinf)(float) = sinf;
+    float (*volatile p_cosf)(float) = cosf;
+    const float tscale = p_powf(hp.rope_theta, -2.0f / (float)HEAD_DIM);
+    for (uint32_t pos = 0; pos < ctx; pos++)
+      for (int p = 0; p < 32; p++) {
+        const float theta = (float)pos * __builtin_powif(tscale, p);
+        t[(size_t)pos * 32 + p] = make_float2(p_cosf(theta), p_sinf(theta));
+      }
+    rope = dalloc<float2>(state_allocs, t.size());
+    CK(cudaMemcpy(rope, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  }
+  x = dalloc<float>(state_allocs, DIM);
+  qkv = dalloc<float>(state_allocs, DIM + 2 * KV_HEADS * HEAD_DIM);
+  a = dalloc<float>(state_allocs, DIM);
+  gated = dalloc<float>(state_allocs, DIM);
+  sw = dalloc<float>(state_allocs, std::max(N_FF, N_USED * EXPERT_FF));
+  down = dalloc<float>(state_allocs, N_USED * DIM);
+  logits = dalloc<float>(state_allocs, hp.vocab);
+  const int nsplit = (ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
+  attn_part = dalloc<float>(state_allocs, (size_t)KV_HEADS * nsplit * 4 * (HEAD_DIM + 2));
+  sel = dalloc<int>(state_allocs, 8);
+  selw = dalloc<float>(state_allocs, 8);
+  io = dalloc<int>(state_allocs, 4);
+  counters = dalloc<unsigned>(state_allocs, 1024);
+  CK(cudaMemsetAsync(counters, 0, 1024 * 4, stream));
+  am_part = dalloc<float2>(state_allocs, 4096);
+  CK(cudaStreamSynchronize(stream));
+  state_ready = true;
+  state_ctx = ctx;
+}
+
+void EngineImpl::ensure_prefill(int n) {
+  if (n <= ncap) return;
+  free_prefill();
+  const int cap = std::max(n, (int)LFM_PREFILL_CHUNK);
+  const size_t N = cap;
+  px = dalloc<float>(prefill_allocs, N * DIM);
+  ph = dalloc<float>(prefill_allocs, N * DIM);
+  pqkv = dalloc<float>(prefill_allocs, N * (DIM + 2 * KV_HEADS * HEAD_DIM));
+  pa = dalloc<float>(prefill_allocs, N * DIM);
+  pbcx = dalloc<float>(prefill_allocs, N * 3 * DIM);
+  pgated = dalloc<float>(prefill_allocs, N * DIM);
+  const size_t wide = std::max<size_t>(N * N_FF, N * N_USED * EXPERT_FF);
+  pgate = dalloc<float>(prefill_allocs, wide);
+  pup = dalloc<float>(prefill_allocs, wide);
+  psw = dalloc<float>(prefill_allocs, wide);
+  pdown = dalloc<float>(prefill_allocs, N * N_USED * DIM);
+  prlog = dalloc<float>(prefill_allocs, N * N_EXPERT);
+  psel = dalloc<int>(prefill_allocs, N * N_USED);
+  pselw = dalloc<float>(prefill_allocs, N * N_USED);
+  pgroups = dalloc<int>(prefill_allocs, (size_t)N_EXPERT * (N + 1));
+  pids = dalloc<uint32_t>(prefill_allocs, N);
+  ncap = cap;
+}
+
+// One decode step for the token/position in io[0], io[1]; next token -> io[2].
+void EngineImpl::enqueue_decode(cudaStream_t s, bool pdl_on) {
+  LaunchCfg c;
+  c.stream = s;
+  c.pdl = pdl_on;
+  c.sms = sms;
+  int n = 0;
+  const float eps = hp.eps;
+  embed_token(embd, io + 0, x, c);
+  n++;
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const LayerW& L = layers[l];
+    const XSrc xa{x, L.attn_norm, eps};
+    if (L.attn) {
+      mv_plain(L.q, xa, qkv, c);
+      mv_plain(L.k, xa, qkv + DIM, c);
+      mv_plain(L.v, xa, qkv + DIM + KV_HEADS * HEAD_DIM, c);
+      AttnDecodeArgs aa;
+      aa.qkv = qkv;
+      aa.q_norm = L.q_norm;
+      aa.k_norm = L.k_norm;
+      aa.rope = rope;
+      aa.pos = io + 1;
+      aa.kc = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      aa.vc = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      aa.part = attn_part;
+      aa.counters = counters + 8 * L.attn_idx;
+      aa.out = a;
+      aa.ctx = (int)ctx;
+      aa.eps = eps;
+      attn_decode(aa, c);
+      mv_resid(L.o, XSrc{a, nullptr, 0.f}, x, c);
+      n += 5;
+    } else {
+      mv_conv(L.in_proj, xa, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, gated, c);
+      mv_resid(L.out_proj, XSrc{gated, nullptr, 0.f}, x, c);
+      n += 2;
+    }
+    const XSrc xf{x, L.ffn_norm, eps};
+    if (L.dense) {
+      mv_swiglu(L.gate, L.up, xf, sw, c);
+      mv_down7168_resid(L.down, sw, x, c);
+      n += 2;
+    } else {
+      router_top4(L.router, L.bias, xf, sel, selw, c);
+      mv_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, c);
+      mv_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, x, counters + 64 + L.moe_idx, c);
+      n += 3;
+    }
+  }
+  mv_lmhead(embd, XSrc{x, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
+  n++;
+  launches_per_decode = n;
+}
+
+void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
+  h_io[0] = (int)token;
+  h_io[1] = (int)pos;
+  CK(cudaEventRecord(ev0, stream));
+  if (use_graph) {
+    if (!graph) {
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+      cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream);
+      enqueue_decode(stream, pdl);
+      cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, stream);
+      CK(cudaStreamEndCapture(stream, &g));
+      cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
+      cudaGraphDestroy(g);
+      CK(e);
+      ctr.graph_captures++;
+    } else {
+      ctr.graph_replays++;
+    }
+    CK(cudaGraphLaunch(graph, stream));
+  } else {
+    CK(cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream));
+    enqueue_decode(stream, pdl);
+    CK(cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, stream));
+  }
+  CK(cudaEventRecord(ev1, stream));
+  CK(cudaStreamSynchronize(stream));
+  CK(cudaGetLastError());
+  CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  ctr.kernel_launches += launches_per_decode;
+  ctr.gpu_argmax++;
+}
+
+namespace {
+// Feed the previous step's argmax back as the next input token (the
+// device-side position scalar of the reference's replayed decode,
+// kernels.rs:648-652) and record it.
+__global__ void k_advance(int* io, uint32_t* rec) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int next = io[2];
+  rec[io[3]] = (uint32_t)next;
+  io[3] += 1;
+  io[0] = next;
+  io[1] += 1;
+}
+}  // namespace
+
+// `steps` decode steps, each consuming the previous step's argmax, with no host
+// round trip in between; out_tokens receives the argmax of every step.
+void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
+  if (steps > loop_cap) {
+    if (loop_tokens) cudaFree(loop_tokens);
+    CK(cudaMalloc(&loop_tokens, (size_t)steps * 4));
+    loop_cap = steps;
+    if (loop_graph) {
+      cudaGraphExecDestroy(loop_graph);
+      loop_graph = nullptr;
+    }
+  }
+  if (!loop_graph) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    k_advance<<<1, 1, 0, stream>>>(io, loop_tokens);
+    enqueue_decode(stream, pdl);
+    CK(cudaStreamEndCapture(stream, &g));
+    cudaError_t e = cudaGraphInstantiate(&loop_graph, g, 0);
+    cudaGraphDestroy(g);
+    CK(e);
+    ctr.graph_captures++;
+  }
+  // io[0..2] hold the last decode step (token, position, next); io[3] = 0.
+  CK(cudaMemsetAsync(io + 3, 0, 4, stream));
+  CK(cudaEventRecord(ev0, stream));
+  for (uint32_t i = 0; i < steps; i++) CK(cudaGraphLaunch(loop_graph, stream));
+  CK(cudaEventRecord(ev1, stream));
+  CK(cudaMemcpyAsync(out_tokens, loop_tokens, (size_t)steps * 4, cudaMemcpyDeviceToHost, stream));
+  CK(cudaStreamSynchronize(stream));
+  CK(cudaGetLastError());
+  CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  ctr.graph_replays += steps;
+  ctr.kernel_launches += (uint64_t)steps * (launches_per_decode + 1);
+  ctr.gpu_argmax += steps;
+}
+
+// n > 1 tokens starting at `start` (resident_graph.rs:226-551 with n columns).
+void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
+  ensure_prefill(n);
+  cudaStream_t s = stream;
+  const float eps = hp.eps;
+  int nl = 0;
+  CK(cudaEventRecord(ev0, s));
+  CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  embed_n(embd, pids, n, px, s);
+  nl++;
+  LaunchCfg c;
+  c.stream = s;
+  c.pdl = false;
+  c.sms = sms;
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const LayerW& L = layers[l];
+    rmsnorm_n(px, L.attn_norm, eps, n, ph, s);
+    nl++;
+    if (L.attn) {
+      const int ld = DIM + 2 * KV_HEADS * HEAD_DIM;
+      gemm_q6_ld(L.q, ph, n, pqkv, ld, false, s);
+      gemm_q6_ld(L.k, ph, n, pqkv + DIM, ld, false, s);
+      gemm_q6_ld(L.v, ph, n, pqkv + DIM + KV_HEADS * HEAD_DIM, ld, false, s);
+      __half* kcl = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      __half* vcl = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kcl, vcl, s);
+      attn_prefill(pqkv, kcl, vcl, start, n, ctx, pa, s);
+      gemm_q6(L.o, pa, n, px, true, s);
+      nl += 6;
+    } else {
+      gemm_q6(L.in_proj, ph, n, pbcx, false, s);
+      conv_prefill(pbcx, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, n, pgated, s);
+      gemm_q6(L.out_proj, pgated, n, px, true, s);
+      nl += 3;
+    }
+    const bool last = l == hp.n_layers - 1;
+    if (last) {
+      // The last layer's FFN only runs on the last token (lfm.rs:540-541).
+      float* xl = px + (size_t)(n - 1) * DIM;
+      const XSrc xf{xl, L.ffn_norm, eps};
+      if (L.dense) {
+        mv_swiglu(L.gate, L.up, xf, sw, c);
+        mv_down7168_resid(L.down, sw, xl, c);
+        nl += 2;
+      } else {
+        router_top4(L.router, L.bias, xf, sel, selw, c);
+        mv_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, c);
+        mv_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, xl, counters + 64 + L.moe_idx, c);
+        nl += 3;
+      }
+      continue;
+    }
+    rmsnorm_n(px, L.ffn_norm, eps, n, ph, s);
+    nl++;
+    if (L.dense) {
+      gemm_q6(L.gate, ph, n, pgate, false, s);
+      gemm_q6(L.up, ph, n, pup, false, s);
+      swiglu_n(pgate, pup, (size_t)n * N_FF, psw, s);
+      gemm_q6(L.down, psw, n, px, true, s);
+      nl += 4;
+    } else {
+      router_logits_n(L.router, ph, n, prlog, s);
+      route_n(prlog, L.bias, N_EXPERT, n, psel, pselw, s);
+      expert_groups(psel, n, pgroups, n, s);
+      gemm_q6_grouped(L.gate_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pgate, s);
+      gemm_q6_grouped(L.up_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pup, s);
+      swiglu_n(pgate, pup, (size_t)n * N_USED * EXPERT_FF, psw, s);
+      gemm_q6_grouped(L.down_x, DIM, psw, 1, pgroups, n, n, pdown, s);
+      combine_n(pdown, pselw, n, px, s);
+      nl += 8;
+      ctr.expert_grouped_launches += 3;
+    }
+  }
+  mv_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
+  nl++;
+  CK(cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(ev1, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaGetLastError());
+  CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  ctr.kernel_launches += nl;
+  ctr.gpu_argmax++;
+  ctr.prefill_tokens += n;
+}
+
+std::vector<uint8_t> EngineImpl::snapshot(uint32_t valid) {
+  std::vector<uint8_t> out;
+  std::vector<__half> hk, hv;
+  std::vector<float> conv(DIM * 2);
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const LayerW& L = layers[l];
+    if (L.attn) {
+      const size_t width = KV_HEADS * HEAD_DIM;
+      hk.resize((size_t)KV_HEADS * valid * HEAD_DIM);
+      hv.resize(hk.size());
+      for (int kh = 0; kh < KV_HEADS; kh++) {
+        const size_t off = ((size_t)L.attn_idx * KV_HEADS + kh) * ctx * HEAD_DIM;
+        CK(cudaMemcpy(hk.data() + (size_t)kh * valid * HEAD_DIM, kc + off, (size_t)valid * HEAD_DIM * 2,
+                      cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(hv.data() + (size_t)kh * valid * HEAD_DIM, vc + off, (size_t)valid * HEAD_DIM * 2,
+                      cudaMemcpyDeviceToHost));
+      }
+      for (int which = 0; which < 2; which++) {
+        const std::vector<__half>& h = which ? hv : hk;
+        const size_t base = out.size();
+        out.resize(base + (size_t)valid * width * 4);
+        float* o = (float*)(out.data() + base);
+        for (uint32_t p = 0; p < valid; p++)
+          for (int kh = 0; kh < KV_HEADS; kh++)
+            for (int d = 0; d < HEAD_DIM; d++)
+              o[(size_t)p * width + kh * HEAD_DIM + d] = __half2float(h[((size_t)kh * valid + p) * HEAD_DIM + d]);
+      }
+    } else {
+      CK(cudaMemcpy(conv.data(), conv_state + (size_t)L.conv_idx * DIM * 2, DIM * 2 * 4, cudaMemcpyDeviceToHost));
+      const size_t base = out.size();
+      out.resize(base + DIM * 2 * 4);
+      memcpy(out.data() + base, conv.data(), DIM * 2 * 4);
+    }
+  }
+  return out;
+}
+
+void EngineImpl::restore(uint32_t valid, const uint8_t* buf, size_t len) {
+  size_t off = 0;
+  std::vector<__half> hk;
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const LayerW& L = layers[l];
+    if (L.attn) {
+      const size_t width = KV_HEADS * HEAD_DIM;
+      const size_t size = (size_t)valid * width * 4;
+      for (int which = 0; which < 2; which++) {
+        if (off + size > len) throw std::runtime_error("truncated snapshot");
+        const float* src = (const float*)(buf + off);
+        hk.resize((size_t)KV_HEADS * valid * HEAD_DIM);
+        for (uint32_t p = 0; p < valid; p++)
+          for (int kh = 0; kh < KV_HEADS; kh++)
+            for (int d = 0; d < HEAD_DIM; d++)
+              hk[((size_t)kh * valid + p) * HEAD_DIM + d] = __float2half_rn(src[(size_t)p * width + kh * HEAD_DIM + d]);
+        __half* dst = which ? vc : kc;
+        for (int kh = 0; kh < KV_HEADS; kh++) {
+          const size_t doff = ((size_t)L.attn_idx * KV_HEADS + kh) * ctx * HEAD_DIM;
+          if (valid)
+            CK(cudaMemcpy(dst + doff, hk.data() + (size_t)kh * valid * HEAD_DIM, (size_t)valid * HEAD_DIM * 2,
+                          cudaMemcpyHostToDevice));
+        }
+        off += size;
+      }
+    } else {
+      const size_t size = DIM * 2 * 4;
+      if (off + size > len) throw std::runtime_error("truncated snapshot");
+      CK(cudaMemcpy(conv_state + (size_t)L.conv_idx * DIM * 2, buf + off, size, cudaMemcpyHostToDevice));
+      off += size;
+    }
+  }
+  if (off != len) throw std::runtime_error("extra snapshot data");
+}
+
+}  // namespace lfm
+
+// =========================================================== C ABI
+using lfm::EngineImpl;
+
+struct lfm_engine {
+  EngineImpl impl;
+};
+
+namespace {
+
+template <class F>
+lfm_status guarded(lfm_engine* e, F&& f) {
+  if (!e) {
+    lfm::g_error = "null engine";
+    return LFM_ERR_ARG;
+  }
+  try {
+    cudaSetDevice(e->impl.device);
+    return f();
+  } catch (const lfm::CudaError& ce) {
+    lfm::set_err(&e->impl, std::string("CUDA: ") + cudaGetErrorString(ce.e));
+    return LFM_ERR_CUDA;
+  } catch (const std::exception& ex) {
+    lfm::set_err(&e->impl, ex.what());
+    return LFM_ERR_ARG;
+  }
+}
+
+lfm_status check_ids(lfm_engine* e, const uint32_t* ids, uint32_t n, int64_t start) {
+  EngineImpl& I = e->impl;
+  if (!ids || n == 0 || start < 0 || (uint64_t)start + n > I.ctx) {
+    lfm::set_err(&I, "forward context range");
+    return LFM_ERR_ARG;
+  }
+  for (uint32_t i = 0; i < n; i++)
+    if (ids[i] >= I.hp.vocab) {
+      lfm::set_err(&I, "token out of range");
+      return LFM_ERR_ARG;
+    }
+  return LFM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out) {
+  if (!gguf_path || !out) {
+    lfm::g_error = "null argument";
+    return LFM_ERR_ARG;
+  }
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    lfm::g_error = "no CUDA device " + std::to_string(device);
+    return LFM_ERR_CUDA;
+  }
+  auto* e = new lfm_engine();
+  EngineImpl& I = e->impl;
+  I.device = device;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    lfm::g_error = "cudaSetDevice failed";
+    delete e;
+    return LFM_ERR_CUDA;
+  }
+  cudaDeviceProp prop;
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major != 10) {
+    lfm::g_error = std::string("device ") + prop.name + " is not sm_100 (B200)";
+    delete e;
+    return LFM_ERR_CUDA;
+  }
+  I.name = prop.name;
+  I.sms = prop.multiProcessorCount;
+  if (const char* v = getenv("LFM_PDL")) I.pdl = std::string(v) != "0";
+  if (const char* v = getenv("LFM_GRAPH")) I.use_graph = std::string(v) != "0";
+  if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMallocHost(&I.h_io, 64) != cudaSuccess || cudaEventCreate(&I.ev0) != cudaSuccess ||
+      cudaEventCreate(&I.ev1) != cudaSuccess) {
+    lfm::g_error = "stream / pinned allocation failed";
+    delete e;
+    return LFM_ERR_CUDA;
+  }
+  if (!I.load(gguf_path)) {
+    lfm::g_error = I.err;
+    delete e;
+    return LFM_ERR_MODEL;
+  }
+  *out = e;
+  return LFM_OK;
+}
+
+void lfm_engine_destroy(lfm_engine* e) { delete e; }
+
+lfm_status lfm_engine_set_ctx(lfm_engine* e, uint32_t ctx) {
+  return guarded(e, [&]() -> lfm_status {
+    if (ctx == 0 || ctx > LFM_MAX_CTX) {
+      lfm::set_err(&e->impl, "context must be 1..4096");
+      return LFM_ERR_ARG;
+    }
+    e->impl.ctx = ctx;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_hparams_get(lfm_engine* e, lfm_hparams* out) {
+  if (!e || !out) return LFM_ERR_ARG;
+  *out = e->impl.hp;
+  return LFM_OK;
+}
+
+lfm_status lfm_forward_token(lfm_engine* e, const uint32_t* ids, uint32_t n, uint32_t position,
+                             uint32_t* next_token) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (n == 0 || n > LFM_PREFILL_CHUNK) {
+      lfm::set_err(&I, "token batch must be 1..64");
+      return LFM_ERR_ARG;
+    }
+    lfm_status st = check_ids(e, ids, n, position);
+    if (st) return st;
+    I.ensure_state();
+    if (n == 1) I.run_decode(ids[0], position);
+    else I.run_prefill(ids, (int)n, position);
+    if (next_token) *next_token = (uint32_t)I.h_io[2];
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_forward_logits(lfm_engine* e, const uint32_t* ids, uint32_t n, int64_t start_pos, float* logits) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    lfm_status st = check_ids(e, ids, n, start_pos);
+    if (st) return st;
+    I.ensure_state();
+    if (n == 1) I.run_decode(ids[0], (uint32_t)start_pos);
+    else I.run_prefill(ids, (int)n, (uint32_t)start_pos);
+    if (logits) CK(cudaMemcpy(logits, I.logits, (size_t)I.hp.vocab * 4, cudaMemcpyDeviceToHost));
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_generate(lfm_engine* e, const uint32_t* prompt, uint32_t prompt_len, uint32_t n, uint32_t eos,
+                        uint32_t* out_tokens, uint32_t* n_out) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!prompt || prompt_len == 0 || (uint64_t)prompt_len + n > I.ctx || (n && !out_tokens)) {
+      lfm::set_err(&I, "empty prompt or context exceeded");
+      return LFM_ERR_ARG;
+    }
+    lfm_status st = check_ids(e, prompt, prompt_len, 0);
+    if (st) return st;
+    I.ensure_state();
+    uint32_t pos = 0, next = 0;
+    for (uint32_t off = 0; off < prompt_len; off += LFM_PREFILL_CHUNK) {
+      const uint32_t c = std::min(LFM_PREFILL_CHUNK, prompt_len - off);
+      if (c == 1) I.run_decode(prompt[off], pos);
+      else I.run_prefill(prompt + off, (int)c, pos);
+      next = (uint32_t)I.h_io[2];
+      pos += c;
+    }
+    uint32_t cnt = 0;
+    for (uint32_t i = 0; i < n; i++) {
+      if (next == eos) break;
+      out_tokens[cnt++] = next;
+      I.run_decode(next, pos);
+      next = (uint32_t)I.h_io[2];
+      pos++;
+    }
+    if (n_out) *n_out = cnt;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_pos, uint32_t steps,
+                           uint32_t* out_tokens, float* device_ms) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!out_tokens || steps == 0 || (uint64_t)start_pos + steps > I.ctx) {
+      lfm::set_err(&I, "forward context range");
+      return LFM_ERR_ARG;
+    }
+    lfm_status st = check_ids(e, &first_token, 1, start_pos);
+    if (st) return st;
+    I.ensure_state();
+    I.run_decode(first_token, start_pos);
+    out_tokens[0] = (uint32_t)I.h_io[2];
+    float first_ms = I.last_ms;
+    if (steps > 1) I.run_loop(steps - 1, out_tokens + 1);
+    if (device_ms) *device_ms = steps > 1 ? I.last_ms : first_ms;
+    return LFM_OK;
+  });
+}
+
+float lfm_last_device_ms(lfm_engine* e) { return e ? e->impl.last_ms : 0.f; }
+
+lfm_status lfm_reset_session(lfm_engine* e) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (I.state_ready) {
+      CK(cudaMemsetAsync(I.conv_state, 0, (size_t)std::max(I.n_conv, 1) * lfm::DIM * 2 * 4, I.stream));
+      CK(cudaStreamSynchronize(I.stream));
+    }
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_snapshot_cache(lfm_engine* e, uint32_t valid, uint8_t* buf, size_t cap, size_t* len) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!I.state_ready) {
+      lfm::set_err(&I, "no resident state");
+      return LFM_ERR_STATE;
+    }
+    if (valid > I.ctx) {
+      lfm::set_err(&I, "snapshot range");
+      return LFM_ERR_ARG;
+    }
+    const size_t need = (size_t)I.n_attn * 2 * valid * lfm::KV_HEADS * lfm::HEAD_DIM * 4 +
+                        (size_t)I.n_conv * lfm::DIM * 2 * 4;
+    if (len) *len = need;
+    if (!buf) return LFM_OK;
+    if (cap < need) {
+      lfm::set_err(&I, "snapshot buffer too small");
+      return LFM_ERR_ARG;
+    }
+    std::vector<uint8_t> v = I.snapshot(valid);
+    memcpy(buf, v.data(), v.size());
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_restore_cache(lfm_engine* e, uint32_t valid, const uint8_t* buf, size_t len) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (valid > I.ctx || (!buf && len)) {
+      lfm::set_err(&I, "restore context");
+      return LFM_ERR_ARG;
+    }
+    I.ensure_state();
+    I.restore(valid, buf, len);
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_snapshot_logits(lfm_engine* e, float* logits) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!I.state_ready || !logits) {
+      lfm::set_err(&I, "no resident state");
+      return LFM_ERR_STATE;
+    }
+    CK(cudaMemcpy(logits, I.logits, (size_t)I.hp.vocab * 4, cudaMemcpyDeviceToHost));
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_counters_get(lfm_engine* e, lfm_counters* out) {
+  if (!e || !out) return LFM_ERR_ARG;
+  *out = e->impl.ctr;
+  return LFM_OK;
+}
+
+const char* lfm_device_name(lfm_engine* e) { return e ? e->impl.name.c_str() : ""; }
+const char* lfm_last_error(lfm_engine* e) { return e ? e->impl.err.c_str() : lfm::g_error.c_str(); }
+const char* lfm_global_error(void) { return lfm::g_error.c_str(); }
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+// Kernel-level C ABI (include/lfm_cuda.h, "kernel-level entry points"): the
+// per-kernel surface of the reference's GpuOps (engine/src/ops.rs:56-575),
+// on caller-owned device pointers. Used by the parity tests and the Q6_K
+// matvec microbench.
+#include <cuda_runtime.h>
+
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/lfm_cuda.h"
+#include "kernels.h"
+
+namespace {
+thread_local std::string t_err;
+
+lfm_status cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return LFM_OK;
+  t_err = std::string("CUDA: ") + cudaGetErrorString(e);
+  return LFM_ERR_CUDA;
+}
+
+bool shape_ok(uint32_t in_dim, uint32_t rows) { return in_dim >= 256 && in_dim % 256 == 0 && rows > 0; }
+}  // namespace
+
+extern "C" {
+
+size_t lfm_q6k_device_bytes(uint32_t in_dim, uint32_t rows) {
+  if (!shape_ok(in_dim, rows)) return 0;
+  return lfm::q6_total_bytes(rows, (int)(in_dim / 256));
+}
+
+lfm_status lfm_q6k_upload(const uint8_t* gguf_rows, uint32_t in_dim, uint32_t rows, void* dst_dev) {
+  if (!gguf_rows || !dst_dev || !shape_ok(in_dim, rows)) {
+    t_err = "lfm_q6k_upload: bad argument";
+    return LFM_ERR_ARG;
+  }
+  const int nb = (int)(in_dim / 256);
+  const size_t bytes = lfm::q6_total_bytes(rows, nb);
+  std::vector<uint8_t> dst(bytes);
+  const unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> th;
+  const size_t per = (rows + nt - 1) / nt;
+  for (unsigned i = 0; i < nt; i++) {
+    const size_t r0 = i * per;
+    if (r0 >= rows) break;
+    const size_t r1 = std::min<size_t>(rows, r0 + per);
+    th.emplace_back([&, r0, r1] { lfm::q6_repack_rows(gguf_rows + r0 * nb * lfm::QB, r0, r1 - r0, nb, rows, dst.data()); });
+  }
+  for (auto& t : th) t.join();
+  return cuda_status(cudaMemcpy(dst_dev, dst.data(), bytes, cudaMemcpyHostToDevice));
+}
+
+lfm_status lfm_q6k_dequant(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t row0, uint32_t nrows,
+                           float* out_dev, void* stream) {
+  if (!w_dev || !out_dev || !shape_ok(in_dim, rows) || row0 + nrows > rows) {
+    t_err = "lfm_q6k_dequant: bad argument";
+    return LFM_ERR_ARG;
+  }
+  if (nrows == 0) return LFM_OK;
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
+  lfm::q6_dequant_rows(W, (int)row0, (int)nrows, out_dev, (cudaStream_t)stream);
+  return cuda_status(cudaGetLastError());
+}
+
+lfm_status lfm_q6k_matmul(const void* w_dev, uint32_t in_dim, uint32_t rows, const float* x_dev, uint32_t n,
+                          float* y_dev, void* stream) {
+  if (!w_dev || !x_dev || !y_dev || !shape_ok(in_dim, rows) || n == 0) {
+    t_err = "lfm_q6k_matmul: bad argument";
+    return LFM_ERR_ARG;
+  }
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
+  if (n == 1 && in_dim <= 2048) {
+    lfm::LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    lfm::mv_plain(W, lfm::XSrc{x_dev, nullptr, 0.f}, y_dev, c);
+  } else {
+    lfm::gemm_q6(W, x_dev, (int)n, y_dev, false, (cudaStream_t)stream);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+lfm_status lfm_q6k_routed(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t n_expert,
+                          const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_stride, float* y_dev,
+                          void* stream) {
+  if (!w_dev || !x_dev || !y_dev || !expert_ids_dev || !shape_ok(in_dim, rows) || in_dim > 2048 ||
+      n_expert == 0 || x_stride < in_dim) {
+    t_err = "lfm_q6k_routed: bad argument (in_dim must be <= 2048)";
+    return LFM_ERR_ARG;
+  }
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)(rows * n_expert), (int)(in_dim / 256));
+  lfm::LaunchCfg c;
+  c.stream = (cudaStream_t)stream;
+  lfm::mv_routed(W, (int)rows, x_dev, (int)x_stride, expert_ids_dev, y_dev, c);
+  return cuda_status(cudaGetLastError());
+}
+
+lfm_status lfm_route(const float* logits_dev, const float* bias_dev, uint32_t n_expert, uint32_t n,
+                     int32_t* sel_ids_dev, float* sel_w_dev, void* stream) {
+  if (!logits_dev || !bias_dev || !sel_ids_dev || !sel_w_dev || n_expert < 4 || n_expert > 32 || n == 0) {
+    t_err = "lfm_route: bad argument (4 <= n_expert <= 32)";
+    return LFM_ERR_ARG;
+  }
+  lfm::route_n(logits_dev, bias_dev, (int)n_expert, (int)n, sel_ids_dev, sel_w_dev, (cudaStream_t)stream);
+  return cuda_status(cudaGetLastError());
+}
+
+lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream) {
+  if (!x_dev || !out_dev || n == 0) {
+    t_err = "lfm_argmax: bad argument";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  // Scratch: up to 256 per-CTA partial maxima and the last-CTA counter.
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(&scratch, 256 * sizeof(float2) + 16, s);
+  if (e != cudaSuccess) return cuda_status(e);
+  unsigned* counter = (unsigned*)((char*)scratch + 256 * sizeof(float2));
+  cudaMemsetAsync(counter, 0, 4, s);
+  lfm::argmax_f32(x_dev, (int)n, (float2*)scratch, counter, (int*)out_dev, s);
+  e = cudaGetLastError();
+  cudaFreeAsync(scratch, s);
+  return cuda_status(e);
+}
+
+const char* lfm_ops_error(void) { return t_err.c_str(); }
+
+}  // extern "C"

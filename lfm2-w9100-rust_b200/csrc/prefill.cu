@@ -1,0 +1,410 @@
+// Prompt (n > 1) kernels: the reference's batched graph
+// (gpu_lfm/resident_graph.rs:226-551 with n tokens) on B200.
+//
+// gemm_q6 / gemm_q6_grouped are the exact-arithmetic (FP32 CUDA-core) Q6_K
+// GEMMs: a CTA dequantises a 64-row x 256-k weight tile (one super-block per
+// row) into shared memory once and reuses it for 64 tokens, the role of the
+// reference's q6k_prompt tiles (kernels.rs:1039-1044) and of the grouped
+// expert tiles over device-built slot lists (q6k_grouped_compact,
+// kernels/persistent.rs:58-76).
+#include <math.h>
+
+#include "kernels.h"
+
+namespace lfm {
+namespace {
+
+constexpr int GM = 64, GN = 64, GK = 256;
+constexpr int GPAD = 4;  // Xs row padding (floats)
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// GROUPED = false: columns are tokens 0..n-1, X row j, output row j.
+// GROUPED = true : blockIdx.z = expert; columns are that expert's slots.
+template <bool GROUPED>
+__global__ void __launch_bounds__(256) k_gemm_q6(Q6Mat W, int out_rows, const float* X, int n,
+                                                 int ldx, int x_div, const int* groups, int cap,
+                                                 float* out, int ldo, bool resid) {
+  extern __shared__ float smem[];
+  float* Ws = smem;                    // [GK][GM]
+  float* Xs = smem + GK * GM;          // [GK][GN + GPAD]
+  __shared__ int s_slot[GN];
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.x * GM;
+  const int c0 = blockIdx.y * GN;
+  int ncols = n;
+  int wrow0 = 0;
+  if (GROUPED) {
+    const int e = blockIdx.z;
+    const int* g = groups + (size_t)e * (cap + 1);
+    ncols = g[0];
+    if (c0 >= ncols) return;
+    wrow0 = e * out_rows;
+    if (tid < GN) s_slot[tid] = (c0 + tid < ncols) ? g[1 + c0 + tid] : -1;
+  } else {
+    if (tid < GN) s_slot[tid] = (c0 + tid < ncols) ? c0 + tid : -1;
+  }
+  __syncthreads();
+  const int U = 4 * W.nb;
+  const int in = W.nb * QK;
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][4] = {};
+  for (int b = 0; b < W.nb; b++) {
+    // dequantise 64 rows x 4 units of block b
+    {
+      const int r = tid & 63, uu = tid >> 6;  // 4 units
+      const int row = r0 + r;
+      const int u = 4 * b + uu;
+      float w[64];
+      if (row < out_rows) {
+        const size_t grow = (size_t)wrow0 + row;
+        const uint4* qp = W.q + grow * 3 * U + u;
+        q6_unit_dequant(qp[0], qp[U], qp[2 * U], W.sc[grow * U + u],
+                        __half2float(W.d[grow * W.nb + b]), w);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; i++) w[i] = 0.f;
+      }
+      const int kb = q6_unit_base(u) - 256 * b;  // offset within the block
+#pragma unroll
+      for (int m = 0; m < 4; m++)
+#pragma unroll
+        for (int i = 0; i < 16; i++) Ws[(kb + 32 * m + i) * GM + r] = w[m * 16 + i];
+    }
+    // activations: column c, 64 k per thread
+    {
+      const int c = tid & 63, kq = tid >> 6;
+      const int slot = s_slot[c];
+      const float* xrow = slot >= 0 ? X + (size_t)(slot / x_div) * ldx + 256 * b + kq * 64 : nullptr;
+#pragma unroll 4
+      for (int k = 0; k < 64; k += 4) {
+        float4 v = xrow ? *(const float4*)(xrow + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        Xs[(kq * 64 + k + 0) * (GN + GPAD) + c] = v.x;
+        Xs[(kq * 64 + k + 1) * (GN + GPAD) + c] = v.y;
+        Xs[(kq * 64 + k + 2) * (GN + GPAD) + c] = v.z;
+        Xs[(kq * 64 + k + 3) * (GN + GPAD) + c] = v.w;
+      }
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < GK; k++) {
+      const float4 a = *(const float4*)(Ws + k * GM + ty * 4);
+      const float4 x = *(const float4*)(Xs + k * (GN + GPAD) + tx * 4);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], xv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  (void)in;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int slot = s_slot[tx * 4 + j];
+    if (slot < 0) continue;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int row = r0 + ty * 4 + i;
+      if (row >= out_rows) continue;
+      float* o = out + (size_t)slot * ldo + row;
+      if (resid) *o += acc[i][j];
+      else *o = acc[i][j];
+    }
+  }
+}
+
+constexpr size_t GEMM_SMEM = (size_t)GK * GM * 4 + (size_t)GK * (GN + GPAD) * 4;
+
+__global__ void k_embed_n(Q6Mat E, const uint32_t* ids, float* x) {
+  const int j = blockIdx.x, u = threadIdx.x;
+  const int U = 4 * E.nb;
+  if (u >= U) return;
+  const size_t tok = ids[j];
+  const uint4* qp = E.q + tok * 3 * U + u;
+  float w[64];
+  q6_unit_dequant(qp[0], qp[U], qp[2 * U], E.sc[tok * U + u], __half2float(E.d[tok * E.nb + (u >> 2)]), w);
+  float* xo = x + (size_t)j * DIM + q6_unit_base(u);
+#pragma unroll
+  for (int m = 0; m < 4; m++)
+#pragma unroll
+    for (int i = 0; i < 16; i++) xo[32 * m + i] = w[m * 16 + i];
+}
+
+// RMSNorm of each token row (kernels.rs:576-634; lfm.rs:231-244).
+__global__ void __launch_bounds__(256) k_rmsnorm_n(const float* x, const float* w, float eps, float* out) {
+  __shared__ float red[8];
+  const float* xr = x + (size_t)blockIdx.x * DIM;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < DIM; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < 8; i++) t += red[i];
+  const float inv = 1.0f / sqrtf(t / (float)DIM + eps);
+  for (int i = threadIdx.x; i < DIM; i += 256) out[(size_t)blockIdx.x * DIM + i] = xr[i] * inv * w[i];
+}
+
+// Short conv over n tokens, one thread per channel, serial in time like
+// kernels/resident.rs:33-56 (three taps over [state0, state1, b*x]).
+__global__ void k_conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated) {
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= DIM) return;
+  float s0 = state[2 * ch], s1 = state[2 * ch + 1];
+  const float w0 = conv_w[3 * ch], w1 = conv_w[3 * ch + 1], w2 = conv_w[3 * ch + 2];
+  for (int j = 0; j < n; j++) {
+    const float* r = bcx + (size_t)j * 3 * DIM;
+    const float bx = r[ch] * r[2 * DIM + ch];
+    float conv = 0.f;
+    conv += s0 * w0;
+    conv += s1 * w1;
+    conv += bx * w2;
+    gated[(size_t)j * DIM + ch] = r[DIM + ch] * conv;
+    s0 = s1;
+    s1 = bx;
+  }
+  state[2 * ch] = s0;
+  state[2 * ch + 1] = s1;
+}
+
+// Head RMSNorm + NEOX RoPE of q (32 heads) and k (8 heads) in place, then the
+// fp16 K/V cache write at positions start..start+n-1 (lfm.rs:368-393).
+__global__ void k_qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope,
+                            int start, int ctx, float eps, __half* kc, __half* vc) {
+  const int j = blockIdx.x;
+  const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);  // 0..47
+  const int lane = threadIdx.x & 31;
+  const int pos = start + j;
+  float* row = qkv + (size_t)j * (DIM + 2 * KV_HEADS * HEAD_DIM);
+  if (hh < HEADS + KV_HEADS) {
+    const bool isq = hh < HEADS;
+    float* v = isq ? row + hh * HEAD_DIM : row + DIM + (hh - HEADS) * HEAD_DIM;
+    const float* nw = isq ? q_norm : k_norm;
+    float a0 = v[lane], a1 = v[lane + 32];
+    const float ss = warp_sum(a0 * a0 + a1 * a1);
+    const float inv = 1.0f / sqrtf(ss / (float)HEAD_DIM + eps);
+    a0 *= inv * nw[lane];
+    a1 *= inv * nw[lane + 32];
+    const float2 cs = rope[(size_t)pos * 32 + lane];
+    const float r0 = a0 * cs.x - a1 * cs.y, r1 = a0 * cs.y + a1 * cs.x;
+    v[lane] = r0;
+    v[lane + 32] = r1;
+    if (!isq) {
+      const int kh = hh - HEADS;
+      const size_t off = ((size_t)kh * ctx + pos) * HEAD_DIM;
+      kc[off + lane] = __float2half_rn(r0);
+      kc[off + lane + 32] = __float2half_rn(r1);
+    }
+  } else {
+    const int kh = hh - HEADS - KV_HEADS;
+    const float* v = row + DIM + KV_HEADS * HEAD_DIM + kh * HEAD_DIM;
+    const size_t off = ((size_t)kh * ctx + pos) * HEAD_DIM;
+    vc[off + lane] = __float2half_rn(v[lane]);
+    vc[off + lane + 32] = __float2half_rn(v[lane + 32]);
+  }
+}
+
+// Causal GQA attention for n new tokens over the fp16 cache (lfm.rs:395-437):
+// one warp per (token, head), online softmax over 32-position chunks.
+__global__ void __launch_bounds__(256) k_attn_prefill(const float* qkv, const __half* kc, const __half* vc,
+                                                      int start, int n, int ctx, float* out) {
+  __shared__ float sq[8][HEAD_DIM];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 8 + warp;
+  if (gw >= n * HEADS) return;
+  const int j = gw / HEADS, h = gw % HEADS;
+  const int kh = h / (HEADS / KV_HEADS);
+  const int p = start + j;
+  const float* q = qkv + (size_t)j * (DIM + 2 * KV_HEADS * HEAD_DIM) + h * HEAD_DIM;
+  sq[warp][lane] = q[lane];
+  sq[warp][lane + 32] = q[lane + 32];
+  __syncwarp();
+  const __half* kb = kc + (size_t)kh * ctx * HEAD_DIM;
+  const __half* vb = vc + (size_t)kh * ctx * HEAD_DIM;
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int t0 = 0; t0 <= p; t0 += 32) {
+    const int t = t0 + lane;
+    float s = -INFINITY;
+    if (t <= p) {
+      const uint4* kp = (const uint4*)(kb + (size_t)t * HEAD_DIM);
+      float acc = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; c8++) {
+        const uint4 v = kp[c8];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const float2 f = __half22float2(*(const __half2*)&w[jj]);
+          acc = fmaf(f.x, sq[warp][c8 * 8 + 2 * jj], acc);
+          acc = fmaf(f.y, sq[warp][c8 * 8 + 2 * jj + 1], acc);
+        }
+      }
+      s = acc * 0.125f;
+    }
+    const float cm = warp_max(s);
+    const float nm = fmaxf(m, cm);
+    const float scale = expf(m - nm);
+    const float pv = t <= p ? expf(s - nm) : 0.f;
+    l = l * scale + warp_sum(pv);
+    o0 *= scale;
+    o1 *= scale;
+    const int cnt = min(32, p - t0 + 1);
+    for (int i = 0; i < cnt; i++) {
+      const float pi = __shfl_sync(0xffffffffu, pv, i);
+      const __half* vr = vb + (size_t)(t0 + i) * HEAD_DIM;
+      o0 = fmaf(pi, __half2float(vr[lane]), o0);
+      o1 = fmaf(pi, __half2float(vr[lane + 32]), o1);
+    }
+    m = nm;
+  }
+  float* o = out + (size_t)j * DIM + h * HEAD_DIM;
+  o[lane] = o0 / l;
+  o[lane + 32] = o1 / l;
+}
+
+// Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574):
+// one warp per (token, expert), then route_n picks the top 4.
+__global__ void k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= n * N_EXPERT) return;
+  const int j = gw / N_EXPERT, e = gw % N_EXPERT;
+  const float4* w = (const float4*)(Wr + (size_t)e * DIM);
+  const float4* x = (const float4*)(xn + (size_t)j * DIM);
+  float a = 0.f;
+  for (int i = lane; i < DIM / 4; i += 32) {
+    const float4 v = w[i], xv = x[i];
+    a = fmaf(v.x, xv.x, a);
+    a = fmaf(v.y, xv.y, a);
+    a = fmaf(v.z, xv.z, a);
+    a = fmaf(v.w, xv.w, a);
+  }
+  a = warp_sum(a);
+  if (lane == 0) logits[(size_t)j * N_EXPERT + e] = a;
+}
+
+// Stable per-expert slot lists (kernels/persistent.rs:58-76): warp e scans
+// slots (token*4 + rank) in order and appends those routed to e.
+__global__ void k_expert_groups(const int* sel, int n, int* groups, int cap) {
+  const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* g = groups + (size_t)e * (cap + 1);
+  int count = 0;
+  const int total = n * N_USED;
+  for (int s0 = 0; s0 < total; s0 += 32) {
+    const int s = s0 + lane;
+    const bool hit = s < total && sel[s] == e;
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (hit) g[1 + count + __popc(m & ((1u << lane) - 1u))] = s;
+    count += __popc(m);
+  }
+  if (lane == 0) g[0] = count;
+}
+
+__global__ void k_swiglu_n(const float* gate, const float* up, size_t count, float* out) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) {
+    const float g = gate[i];
+    out[i] = g / (1.0f + expf(-g)) * up[i];
+  }
+}
+
+// x[j] += sum_r w[j,r] * down[j*4 + r] in rank order (kernels/resident.rs:101-117).
+__global__ void k_combine_n(const float* down, const float* selw, int n, float* x) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)n * DIM) return;
+  const size_t j = i / DIM, k = i % DIM;
+  float a = 0.f;
+#pragma unroll
+  for (int r = 0; r < N_USED; r++) a += down[(j * N_USED + r) * DIM + k] * selw[j * N_USED + r];
+  x[i] += a;
+}
+
+__global__ void k_add_n(float* x, const float* y, size_t count) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) x[i] += y[i];
+}
+
+}  // namespace
+
+void gemm_q6_ld(const Q6Mat& W, const float* X, int n, float* out, int ldo, bool resid, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_q6<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
+    cudaFuncSetAttribute(k_gemm_q6<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
+    attr = true;
+  }
+  dim3 grid((W.rows + GM - 1) / GM, (n + GN - 1) / GN);
+  k_gemm_q6<false><<<grid, 256, GEMM_SMEM, s>>>(W, W.rows, X, n, W.nb * QK, 1, nullptr, 0, out, ldo, resid);
+}
+
+void gemm_q6(const Q6Mat& W, const float* X, int n, float* out, bool resid, cudaStream_t s) {
+  gemm_q6_ld(W, X, n, out, W.rows, resid, s);
+}
+
+void gemm_q6_grouped(const Q6Mat& W, int out_rows, const float* X, int x_div, const int* groups, int cap,
+                     int max_count, float* out, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_q6<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
+    attr = true;
+  }
+  dim3 grid((out_rows + GM - 1) / GM, (max_count + GN - 1) / GN, N_EXPERT);
+  k_gemm_q6<true><<<grid, 256, GEMM_SMEM, s>>>(W, out_rows, X, 0, W.nb * QK, x_div, groups, cap, out,
+                                               out_rows, false);
+}
+
+void embed_n(const Q6Mat& E, const uint32_t* ids, int n, float* x, cudaStream_t s) {
+  k_embed_n<<<n, 32, 0, s>>>(E, ids, x);
+}
+
+void rmsnorm_n(const float* x, const float* w, float eps, int n, float* out, cudaStream_t s) {
+  k_rmsnorm_n<<<n, 256, 0, s>>>(x, w, eps, out);
+}
+
+void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated, cudaStream_t s) {
+  k_conv_prefill<<<DIM / 128, 128, 0, s>>>(bcx, conv_w, state, n, gated);
+}
+
+void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int start, int n,
+               int ctx, float eps, __half* kc, __half* vc, cudaStream_t s) {
+  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, start, ctx, eps, kc, vc);
+}
+
+void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int start, int n, int ctx, float* out,
+                  cudaStream_t s) {
+  k_attn_prefill<<<(n * HEADS + 7) / 8, 256, 0, s>>>(qkv, kc, vc, start, n, ctx, out);
+}
+
+void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
+  k_router_logits_n<<<(n * N_EXPERT + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
+}
+
+void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {
+  k_expert_groups<<<1, N_EXPERT * 32, 0, s>>>(sel, n, groups, cap);
+}
+
+void swiglu_n(const float* gate, const float* up, size_t count, float* out, cudaStream_t s) {
+  k_swiglu_n<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(gate, up, count, out);
+}
+
+void combine_n(const float* down, const float* selw, int n, float* x, cudaStream_t s) {
+  const size_t count = (size_t)n * DIM;
+  k_combine_n<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(down, selw, n, x);
+}
+
+void add_n(float* x, const float* y, size_t count, cudaStream_t s) {
+  k_add_n<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(x, y, count);
+}
+
+}  // namespace lfm

@@ -1,0 +1,201 @@
+"""Python binding of liblfm2_b200.so (include/lfm_cuda.h) through ctypes.
+
+`GpuEngine` mirrors the reference's `lfm2_engine::gpu_lfm::GpuEngine`
+(engine/src/gpu_lfm.rs:23-245, engine/src/gpu_lfm/resident_graph.rs:90-602):
+load, set_ctx, forward (full logits), forward_token (device argmax),
+reset_session, snapshot/restore of the resident cache, snapshot of the last
+logits. There is no CPU fallback: if the CUDA library cannot be loaded, every
+call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblfm2_b200.so")
+
+VOCAB = 128000
+PREFILL_CHUNK = 64  # engine/src/work_bound.rs:6
+
+
+class LfmError(RuntimeError):
+    pass
+
+
+class Hparams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("dim", "heads", "head_dim", "n_layers", "vocab", "n_expert", "n_used", "expert_ff",
+                 "n_ff", "dense_lead", "conv_l_cache", "eos")] + \
+               [("eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_heads", ctypes.c_uint32 * 64)]
+
+
+class Counters(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in
+                ("kernel_launches", "gpu_argmax", "graph_replays", "graph_captures", "prefill_tokens",
+                 "expert_grouped_launches")]
+
+
+_lib = None
+
+# Every symbol declared in include/lfm_cuda.h.
+EXPORTS = [
+    "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
+    "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
+    "lfm_reset_session",
+    "lfm_snapshot_cache", "lfm_restore_cache", "lfm_snapshot_logits", "lfm_counters_get",
+    "lfm_device_name", "lfm_last_error", "lfm_global_error", "lfm_q6k_device_bytes",
+    "lfm_q6k_upload", "lfm_q6k_dequant", "lfm_q6k_matmul", "lfm_q6k_routed", "lfm_route",
+    "lfm_argmax", "lfm_ops_error",
+]
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library (fails loudly if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise LfmError(f"{LIB_PATH} is missing: run lfm2-w9100-rust_b200/build.py (no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, U32, I64, SZ = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int64, ctypes.c_size_t
+    st = ctypes.c_int32
+    sig = {
+        "lfm_engine_create": ([ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(P)], st),
+        "lfm_engine_destroy": ([P], None),
+        "lfm_engine_set_ctx": ([P, U32], st),
+        "lfm_hparams_get": ([P, ctypes.POINTER(Hparams)], st),
+        "lfm_forward_logits": ([P, P, U32, I64, P], st),
+        "lfm_forward_token": ([P, P, U32, U32, ctypes.POINTER(U32)], st),
+        "lfm_generate": ([P, P, U32, U32, U32, P, ctypes.POINTER(U32)], st),
+        "lfm_decode_loop": ([P, U32, U32, U32, P, ctypes.POINTER(ctypes.c_float)], st),
+        "lfm_last_device_ms": ([P], ctypes.c_float),
+        "lfm_reset_session": ([P], st),
+        "lfm_snapshot_cache": ([P, U32, P, SZ, ctypes.POINTER(SZ)], st),
+        "lfm_restore_cache": ([P, U32, P, SZ], st),
+        "lfm_snapshot_logits": ([P, P], st),
+        "lfm_counters_get": ([P, ctypes.POINTER(Counters)], st),
+        "lfm_device_name": ([P], ctypes.c_char_p),
+        "lfm_last_error": ([P], ctypes.c_char_p),
+        "lfm_global_error": ([], ctypes.c_char_p),
+        "lfm_q6k_device_bytes": ([U32, U32], SZ),
+        "lfm_q6k_upload": ([P, U32, U32, P], st),
+        "lfm_q6k_dequant": ([P, U32, U32, U32, U32, P, P], st),
+        "lfm_q6k_matmul": ([P, U32, U32, P, U32, P, P], st),
+        "lfm_q6k_routed": ([P, U32, U32, U32, P, P, U32, P, P], st),
+        "lfm_route": ([P, P, U32, U32, P, P, P], st),
+        "lfm_argmax": ([P, U32, P, P], st),
+        "lfm_ops_error": ([], ctypes.c_char_p),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def ops_check(status: int, what: str):
+    if status != 0:
+        raise LfmError(f"{what}: {lib().lfm_ops_error().decode()} (status {status})")
+
+
+class GpuEngine:
+    """The B200 engine behind the C ABI (one per GPU per host thread)."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        h = ctypes.c_void_p()
+        st = lib().lfm_engine_create(gguf_path.encode(), device, ctypes.byref(h))
+        if st != 0:
+            raise LfmError(f"lfm_engine_create: {lib().lfm_global_error().decode()} (status {st})")
+        self.h = h
+        hp = Hparams()
+        lib().lfm_hparams_get(self.h, ctypes.byref(hp))
+        self.hp = hp
+        self.vocab = hp.vocab
+        self.eos = hp.eos
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lfm_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int, what: str):
+        if st != 0:
+            raise LfmError(f"{what}: {lib().lfm_last_error(self.h).decode()} (status {st})")
+
+    @property
+    def device_name(self) -> str:
+        return lib().lfm_device_name(self.h).decode()
+
+    def set_ctx(self, ctx: int):
+        self._check(lib().lfm_engine_set_ctx(self.h, ctx), "set_ctx")
+
+    def forward(self, ids, start_pos: int) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        out = np.empty(self.vocab, dtype=np.float32)
+        self._check(lib().lfm_forward_logits(self.h, _p(ids), ids.size, start_pos, _p(out)), "forward")
+        return out
+
+    def forward_token(self, ids, position: int) -> int:
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        nxt = ctypes.c_uint32()
+        self._check(lib().lfm_forward_token(self.h, _p(ids), ids.size, position, ctypes.byref(nxt)),
+                    "forward_token")
+        return int(nxt.value)
+
+    def generate(self, prompt, n: int, eos: int):
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.empty(max(n, 1), dtype=np.uint32)
+        cnt = ctypes.c_uint32()
+        self._check(lib().lfm_generate(self.h, _p(prompt), prompt.size, n, eos, _p(out), ctypes.byref(cnt)),
+                    "generate")
+        return out[: cnt.value].tolist()
+
+    def decode_loop(self, first_token: int, start_pos: int, steps: int):
+        """Device-resident greedy decode; returns (tokens, device_ms)."""
+        out = np.empty(steps, dtype=np.uint32)
+        ms = ctypes.c_float()
+        self._check(lib().lfm_decode_loop(self.h, first_token, start_pos, steps, _p(out), ctypes.byref(ms)),
+                    "decode_loop")
+        return out.tolist(), float(ms.value)
+
+    def last_device_ms(self) -> float:
+        return float(lib().lfm_last_device_ms(self.h))
+
+    def reset_session(self):
+        self._check(lib().lfm_reset_session(self.h), "reset_session")
+
+    def snapshot_resident_cache(self, valid: int) -> bytes:
+        n = ctypes.c_size_t()
+        self._check(lib().lfm_snapshot_cache(self.h, valid, None, 0, ctypes.byref(n)), "snapshot")
+        buf = np.empty(n.value, dtype=np.uint8)
+        self._check(lib().lfm_snapshot_cache(self.h, valid, _p(buf), buf.size, ctypes.byref(n)), "snapshot")
+        return buf.tobytes()
+
+    def restore_session(self, valid: int, data: bytes):
+        buf = np.frombuffer(data, dtype=np.uint8)
+        self._check(lib().lfm_restore_cache(self.h, valid, _p(buf) if buf.size else None, buf.size), "restore")
+
+    def snapshot_resident_logits(self) -> np.ndarray:
+        out = np.empty(self.vocab, dtype=np.float32)
+        self._check(lib().lfm_snapshot_logits(self.h, _p(out)), "snapshot_logits")
+        return out
+
+    def counters(self) -> dict:
+        c = Counters()
+        lib().lfm_counters_get(self.h, ctypes.byref(c))
+        return {k: int(getattr(c, k)) for k, _ in Counters._fields_}
