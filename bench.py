@@ -112,6 +112,7 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.t.join(timeout=5)
 
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
@@ -279,9 +280,14 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-micro", action="store_true")
+    ap.add_argument("--micro-only", action="store_true", help="only the config-1 Q6_K matvec microbench")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local, pg = dist_setup(args.gpus)
+    if args.micro_only:
+        if rank == 0:
+            print(json.dumps({"microbench": microbench(local)}), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args, ws, rank, pg)
         if pg is not None:
@@ -364,8 +370,8 @@ def main():
     if rank == 0 and not args.no_micro:
         micro = microbench(local)
     cpu = None
+    eng.close()  # release the device before the CPU leg and before interpreter teardown
     if rank == 0 and ws == 1 and not args.no_cpu:
-        eng.close()
         cpu = cpu_baseline(path, 16, 2)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,

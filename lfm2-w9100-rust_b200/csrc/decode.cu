@@ -540,6 +540,36 @@ __global__ void __launch_bounds__(1024) k_router(const float* Wr, const float* b
   if (warp == 0) route_warp(lg[lane], bias, N_EXPERT, lane, sel, selw);
 }
 
+// Router over 32 CTAs (one expert logit each) with the top-4 selection done
+// by the last CTA to finish (deterministic: logits are reduced in a fixed
+// order, the selection reads them back in expert order).
+__global__ void __launch_bounds__(256) k_router_mc(const float* Wr, const float* bias, XSrc xs, float* lg,
+                                                   unsigned* counter, int* sel, float* selw) {
+  __shared__ float red[32];
+  __shared__ bool s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int e = blockIdx.x;
+  const float inv = xs.norm ? rms_inv(xs.x, xs.eps, red) : 1.f;
+  const float* w = Wr + (size_t)e * DIM;
+  float a = 0.f;
+  for (int i = threadIdx.x; i < DIM; i += blockDim.x) {
+    const float xv = xs.norm ? xs.x[i] * inv * xs.norm[i] : xs.x[i];
+    a = fmaf(__ldg(w + i), xv, a);
+  }
+  a = block_sum(a, red);
+  if (threadIdx.x == 0) {
+    lg[e] = a;
+    __threadfence();
+    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (threadIdx.x < 32) route_warp(__ldcg(lg + threadIdx.x), bias, (int)gridDim.x, threadIdx.x, sel, selw);
+  if (threadIdx.x == 0) *counter = 0;
+}
+
 __global__ void k_route_n(const float* logits, const float* bias, int n_expert, int n, int* sel,
                           float* selw) {
   const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -572,16 +602,19 @@ __global__ void k_embed(Q6Mat E, const int* token, float* x) {
 __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
   const int kh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int S = ATTN_SPLIT;   // positions per split (== 32: one per lane)
+  constexpr int KP = HEAD_DIM + 8; // padded fp16 row (conflict-free 16-byte reads)
   __shared__ float sq[4][HEAD_DIM];
-  __shared__ float sp[4][ATTN_SPLIT];
+  __shared__ __align__(16) __half sk[S][KP];
+  __shared__ __align__(16) __half sv[S][HEAD_DIM];
   __shared__ bool s_last;
   pdl_trigger();
   pdl_wait();
   const int pos = *a.pos;
-  const int t0 = split * ATTN_SPLIT;
+  const int t0 = split * S;
   if (t0 > pos) return;
-  const int nact = pos / ATTN_SPLIT + 1;
-  const int nsplit = (a.ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
+  const int nact = pos / S + 1;
+  const int nsplit = (a.ctx + S - 1) / S;
   const int h = kh * (HEADS / KV_HEADS) + warp;  // GQA: kh = h * kv / heads
   const float2 cs = a.rope[(size_t)pos * 32 + lane];
   {
@@ -595,7 +628,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
     sq[warp][lane] = q0 * cs.x - q1 * cs.y;
     sq[warp][lane + 32] = q0 * cs.y + q1 * cs.x;
   }
-  if (pos < t0 + ATTN_SPLIT) {
+  if (pos < t0 + S) {
     // This split holds `pos`: write the new K/V (fp16, RNE) before reading.
     const size_t off = ((size_t)kh * a.ctx + pos) * HEAD_DIM;
     if (warp == 0) {
@@ -611,45 +644,51 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
       a.vc[off + lane] = __float2half_rn(v[lane]);
       a.vc[off + lane + 32] = __float2half_rn(v[lane + 32]);
     }
+    __syncthreads();
+  }
+  const int tend = min(t0 + S, pos + 1);
+  const int cnt = tend - t0;
+  {
+    // stage the K and V tiles (S x 64 fp16 each): 128 threads x 2 x 16 B
+    const uint4* kg = (const uint4*)(a.kc + ((size_t)kh * a.ctx + t0) * HEAD_DIM);
+    const uint4* vg = (const uint4*)(a.vc + ((size_t)kh * a.ctx + t0) * HEAD_DIM);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int idx = threadIdx.x + i * 128;  // 0..255 = 32 rows x 8 chunks
+      const int r = idx >> 3, c = idx & 7;
+      if (r < cnt) {
+        *(uint4*)&sk[r][c * 8] = kg[idx];
+        *(uint4*)&sv[r][c * 8] = vg[idx];
+      }
+    }
   }
   __syncthreads();
-  const int tend = min(t0 + ATTN_SPLIT, pos + 1);
-  float s[2];
+  // scores: lane = position
+  float sc = -INFINITY;
+  if (lane < cnt) {
+    float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < 2; i++) {
-    const int t = t0 + i * 32 + lane;
-    float acc = -INFINITY;
-    if (t < tend) {
-      const uint4* kp = (const uint4*)(a.kc + ((size_t)kh * a.ctx + t) * HEAD_DIM);
-      acc = 0.f;
+    for (int c8 = 0; c8 < 8; c8++) {
+      const uint4 v = *(const uint4*)&sk[lane][c8 * 8];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int c8 = 0; c8 < 8; c8++) {
-        const uint4 v = kp[c8];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float2 f = __half22float2(*(const __half2*)&w[j]);
-          acc = fmaf(f.x, sq[warp][c8 * 8 + 2 * j], acc);
-          acc = fmaf(f.y, sq[warp][c8 * 8 + 2 * j + 1], acc);
-        }
+      for (int j = 0; j < 4; j++) {
+        const float2 f = __half22float2(*(const __half2*)&w[j]);
+        acc = fmaf(f.x, sq[warp][c8 * 8 + 2 * j], acc);
+        acc = fmaf(f.y, sq[warp][c8 * 8 + 2 * j + 1], acc);
       }
-      acc *= 0.125f;  // 1/sqrt(head_dim)
     }
-    s[i] = acc;
+    sc = acc * 0.125f;  // 1/sqrt(head_dim)
   }
-  const float m = warp_max(fmaxf(s[0], s[1]));
-  const float p0 = (t0 + lane < tend) ? expf(s[0] - m) : 0.f;
-  const float p1 = (t0 + 32 + lane < tend) ? expf(s[1] - m) : 0.f;
-  const float l = warp_sum(p0 + p1);
-  sp[warp][lane] = p0;
-  sp[warp][lane + 32] = p1;
-  __syncwarp();
+  const float m = warp_max(sc);
+  const float pl = lane < cnt ? expf(sc - m) : 0.f;
+  const float l = warp_sum(pl);
   float o0 = 0.f, o1 = 0.f;
-  const __half* vbase = a.vc + (size_t)kh * a.ctx * HEAD_DIM;
-  for (int t = t0; t < tend; t++) {
-    const float pt = sp[warp][t - t0];
-    o0 = fmaf(pt, __half2float(vbase[(size_t)t * HEAD_DIM + lane]), o0);
-    o1 = fmaf(pt, __half2float(vbase[(size_t)t * HEAD_DIM + lane + 32]), o1);
+#pragma unroll 8
+  for (int t = 0; t < cnt; t++) {
+    const float pt = __shfl_sync(0xffffffffu, pl, t);
+    o0 = fmaf(pt, __half2float(sv[t][lane]), o0);
+    o1 = fmaf(pt, __half2float(sv[t][lane + 32]), o1);
   }
   float* pp = a.part + (((size_t)kh * nsplit + split) * 4 + warp) * (HEAD_DIM + 2);
   pp[lane] = o0;
@@ -669,7 +708,8 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnDecodeArgs a) {
   // Merge the splits in index order (attention_split.rs:18-33).
   const float* base = a.part + ((size_t)kh * nsplit * 4 + warp) * (HEAD_DIM + 2);
   float M = -INFINITY;
-  for (int sidx = 0; sidx < nact; sidx++) M = fmaxf(M, __ldcg(base + (size_t)sidx * 4 * (HEAD_DIM + 2) + 64));
+  for (int sidx = lane; sidx < nact; sidx += 32) M = fmaxf(M, __ldcg(base + (size_t)sidx * 4 * (HEAD_DIM + 2) + 64));
+  M = warp_max(M);
   float L = 0.f, O0 = 0.f, O1 = 0.f;
   for (int sidx = 0; sidx < nact; sidx++) {
     const float* q = base + (size_t)sidx * 4 * (HEAD_DIM + 2);
@@ -702,6 +742,11 @@ void launch_pdl(K kernel, dim3 grid, dim3 block, const LaunchCfg& c, Args... arg
 void router_top4(const float* Wr, const float* bias, XSrc xs, int* sel, float* selw,
                  const LaunchCfg& c) {
   launch_pdl(k_router, dim3(1), dim3(1024), c, Wr, bias, xs, sel, selw);
+}
+
+void router_top4_mc(const float* Wr, const float* bias, XSrc xs, float* lg_scratch, unsigned* counter, int* sel,
+                    float* selw, const LaunchCfg& c) {
+  launch_pdl(k_router_mc, dim3(N_EXPERT), dim3(256), c, Wr, bias, xs, lg_scratch, counter, sel, selw);
 }
 
 void route_n(const float* logits, const float* bias, int n_expert, int n, int* sel, float* selw,

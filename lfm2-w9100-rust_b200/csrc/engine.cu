@@ -76,8 +76,9 @@ struct EngineImpl {
   std::vector<void*> weight_allocs;
   size_t weight_bytes = 0;
   int n_attn = 0, n_conv = 0, n_moe = 0;
-  bool pdl = true;
+  bool pdl = false;  // programmatic dependent launch between decode kernels (LFM_PDL=1)
   bool use_graph = true;
+  bool use_mvt = true;  // TMA-staged decode matvecs
 
   // resident state
   uint32_t ctx = 4096;
@@ -88,9 +89,9 @@ struct EngineImpl {
   float2* rope = nullptr;
   // decode buffers
   float *x = nullptr, *qkv = nullptr, *a = nullptr, *gated = nullptr, *sw = nullptr, *down = nullptr,
-        *logits = nullptr, *attn_part = nullptr, *selw = nullptr;
+        *logits = nullptr, *attn_part = nullptr, *selw = nullptr, *router_lg = nullptr;
   int* sel = nullptr;
-  int* io = nullptr;  // [0] token, [1] position, [2] next token
+  int* io = nullptr;  // [0] token, [1] position, [2] next token, [3] loop index, [4] device error word
   unsigned* counters = nullptr;
   float2* am_part = nullptr;
   int* h_io = nullptr;  // pinned
@@ -114,8 +115,8 @@ struct EngineImpl {
 
   ~EngineImpl() {
     cudaSetDevice(device);
-    if (graph) cudaGraphExecDestroy(graph);
-    if (loop_graph) cudaGraphExecDestroy(loop_graph);
+    if (stream) cudaStreamSynchronize(stream);
+    // free_state() destroys the graph execs (each exactly once)
     if (loop_tokens) cudaFree(loop_tokens);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
@@ -164,6 +165,8 @@ struct EngineImpl {
 
   // ------------------------------------------------------------- forward
   void enqueue_decode(cudaStream_t s, bool pdl_on);
+  void enqueue_ffn(const LayerW& L, float* xr, const LaunchCfg& c, unsigned* err);
+  void check_device_error();
   void run_decode(uint32_t token, uint32_t pos);
   void run_prefill(const uint32_t* ids, int n, uint32_t start);
   void run_loop(uint32_t steps, uint32_t* out_tokens);
@@ -377,8 +380,10 @@ void EngineImpl::ensure_state() {
   const int nsplit = (ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
   attn_part = dalloc<float>(state_allocs, (size_t)KV_HEADS * nsplit * 4 * (HEAD_DIM + 2));
   sel = dalloc<int>(state_allocs, 8);
+  router_lg = dalloc<float>(state_allocs, N_EXPERT);
   selw = dalloc<float>(state_allocs, 8);
-  io = dalloc<int>(state_allocs, 4);
+  io = dalloc<int>(state_allocs, 8);
+  CK(cudaMemsetAsync(io, 0, 8 * 4, stream));
   counters = dalloc<unsigned>(state_allocs, 1024);
   CK(cudaMemsetAsync(counters, 0, 1024 * 4, stream));
   am_part = dalloc<float2>(state_allocs, 4096);
@@ -419,15 +424,21 @@ void EngineImpl::enqueue_decode(cudaStream_t s, bool pdl_on) {
   c.sms = sms;
   int n = 0;
   const float eps = hp.eps;
+  unsigned* err = (unsigned*)(io + 4);
   embed_token(embd, io + 0, x, c);
   n++;
   for (uint32_t l = 0; l < hp.n_layers; l++) {
     const LayerW& L = layers[l];
     const XSrc xa{x, L.attn_norm, eps};
     if (L.attn) {
-      mv_plain(L.q, xa, qkv, c);
-      mv_plain(L.k, xa, qkv + DIM, c);
-      mv_plain(L.v, xa, qkv + DIM + KV_HEADS * HEAD_DIM, c);
+      if (use_mvt) {
+        mvt_qkv(L.q, L.k, L.v, xa, qkv, err, c);
+        n -= 2;
+      } else {
+        mv_plain(L.q, xa, qkv, c);
+        mv_plain(L.k, xa, qkv + DIM, c);
+        mv_plain(L.v, xa, qkv + DIM + KV_HEADS * HEAD_DIM, c);
+      }
       AttnDecodeArgs aa;
       aa.qkv = qkv;
       aa.q_norm = L.q_norm;
@@ -442,28 +453,47 @@ void EngineImpl::enqueue_decode(cudaStream_t s, bool pdl_on) {
       aa.ctx = (int)ctx;
       aa.eps = eps;
       attn_decode(aa, c);
-      mv_resid(L.o, XSrc{a, nullptr, 0.f}, x, c);
+      if (use_mvt) mvt_resid(L.o, XSrc{a, nullptr, 0.f}, x, err, c);
+      else mv_resid(L.o, XSrc{a, nullptr, 0.f}, x, c);
       n += 5;
     } else {
-      mv_conv(L.in_proj, xa, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, gated, c);
-      mv_resid(L.out_proj, XSrc{gated, nullptr, 0.f}, x, c);
+      float* st = conv_state + (size_t)L.conv_idx * DIM * 2;
+      if (use_mvt) {
+        mvt_conv(L.in_proj, xa, L.conv_w, st, gated, err, c);
+        mvt_resid(L.out_proj, XSrc{gated, nullptr, 0.f}, x, err, c);
+      } else {
+        mv_conv(L.in_proj, xa, L.conv_w, st, gated, c);
+        mv_resid(L.out_proj, XSrc{gated, nullptr, 0.f}, x, c);
+      }
       n += 2;
     }
-    const XSrc xf{x, L.ffn_norm, eps};
-    if (L.dense) {
-      mv_swiglu(L.gate, L.up, xf, sw, c);
-      mv_down7168_resid(L.down, sw, x, c);
-      n += 2;
-    } else {
-      router_top4(L.router, L.bias, xf, sel, selw, c);
-      mv_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, c);
-      mv_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, x, counters + 64 + L.moe_idx, c);
-      n += 3;
-    }
+    enqueue_ffn(L, x, c, err);
+    n += L.dense ? 2 : 3;
   }
-  mv_lmhead(embd, XSrc{x, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
+  if (use_mvt) mvt_lmhead(embd, XSrc{x, out_norm, eps}, logits, am_part, counters + 128, io + 2, err, c);
+  else mv_lmhead(embd, XSrc{x, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
   n++;
   launches_per_decode = n;
+}
+
+// FFN of one token whose residual row is `xr` (decode, and the last token of a
+// prefill: lfm.rs:540-541).
+void EngineImpl::enqueue_ffn(const LayerW& L, float* xr, const LaunchCfg& c, unsigned* err) {
+  const XSrc xf{xr, L.ffn_norm, hp.eps};
+  if (L.dense) {
+    if (use_mvt) mvt_swiglu(L.gate, L.up, xf, sw, err, c);
+    else mv_swiglu(L.gate, L.up, xf, sw, c);
+    mv_down7168_resid(L.down, sw, xr, c);
+  } else {
+    router_top4_mc(L.router, L.bias, xf, router_lg, counters + 160, sel, selw, c);
+    if (use_mvt) {
+      mvt_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, err, c);
+      mvt_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, xr, counters + 64 + L.moe_idx, err, c);
+    } else {
+      mv_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, c);
+      mv_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, xr, counters + 64 + L.moe_idx, c);
+    }
+  }
 }
 
 void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
@@ -476,7 +506,7 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
       CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
       cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream);
       enqueue_decode(stream, pdl);
-      cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, stream);
+      cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, stream);
       CK(cudaStreamEndCapture(stream, &g));
       cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
       cudaGraphDestroy(g);
@@ -489,7 +519,7 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
   } else {
     CK(cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream));
     enqueue_decode(stream, pdl);
-    CK(cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, stream));
+    CK(cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, stream));
   }
   CK(cudaEventRecord(ev1, stream));
   CK(cudaStreamSynchronize(stream));
@@ -497,6 +527,17 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
   CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
   ctr.kernel_launches += launches_per_decode;
   ctr.gpu_argmax++;
+  check_device_error();
+}
+
+// The device error word (io[4]) is raised by a bounded wait that timed out.
+void EngineImpl::check_device_error() {
+  if (h_io[4] != 0) {
+    h_io[4] = 0;
+    cudaMemsetAsync(io + 4, 0, 4, stream);
+    cudaStreamSynchronize(stream);
+    throw std::runtime_error("device status word raised: a bounded wait in a kernel timed out");
+  }
 }
 
 namespace {
@@ -543,9 +584,11 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
   for (uint32_t i = 0; i < steps; i++) CK(cudaGraphLaunch(loop_graph, stream));
   CK(cudaEventRecord(ev1, stream));
   CK(cudaMemcpyAsync(out_tokens, loop_tokens, (size_t)steps * 4, cudaMemcpyDeviceToHost, stream));
+  CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, stream));
   CK(cudaStreamSynchronize(stream));
   CK(cudaGetLastError());
   CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  check_device_error();
   ctr.graph_replays += steps;
   ctr.kernel_launches += (uint64_t)steps * (launches_per_decode + 1);
   ctr.gpu_argmax += steps;
@@ -589,18 +632,8 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
     const bool last = l == hp.n_layers - 1;
     if (last) {
       // The last layer's FFN only runs on the last token (lfm.rs:540-541).
-      float* xl = px + (size_t)(n - 1) * DIM;
-      const XSrc xf{xl, L.ffn_norm, eps};
-      if (L.dense) {
-        mv_swiglu(L.gate, L.up, xf, sw, c);
-        mv_down7168_resid(L.down, sw, xl, c);
-        nl += 2;
-      } else {
-        router_top4(L.router, L.bias, xf, sel, selw, c);
-        mv_expert_swiglu(L.gate_x, L.up_x, EXPERT_FF, xf, sel, sw, c);
-        mv_expert_down(L.down_x, EXPERT_FF, sw, sel, selw, down, xl, counters + 64 + L.moe_idx, c);
-        nl += 3;
-      }
+      enqueue_ffn(L, px + (size_t)(n - 1) * DIM, c, (unsigned*)(io + 4));
+      nl += L.dense ? 2 : 3;
       continue;
     }
     rmsnorm_n(px, L.ffn_norm, eps, n, ph, s);
@@ -624,9 +657,13 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       ctr.expert_grouped_launches += 3;
     }
   }
-  mv_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
+  if (use_mvt)
+    mvt_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2,
+               (unsigned*)(io + 4), c);
+  else
+    mv_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
   nl++;
-  CK(cudaMemcpyAsync(h_io + 2, io + 2, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, s));
   CK(cudaEventRecord(ev1, s));
   CK(cudaStreamSynchronize(s));
   CK(cudaGetLastError());
@@ -634,6 +671,7 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
   ctr.kernel_launches += nl;
   ctr.gpu_argmax++;
   ctr.prefill_tokens += n;
+  check_device_error();
 }
 
 std::vector<uint8_t> EngineImpl::snapshot(uint32_t valid) {
@@ -785,6 +823,7 @@ lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out
   I.sms = prop.multiProcessorCount;
   if (const char* v = getenv("LFM_PDL")) I.pdl = std::string(v) != "0";
   if (const char* v = getenv("LFM_GRAPH")) I.use_graph = std::string(v) != "0";
+  if (const char* v = getenv("LFM_MVT")) I.use_mvt = std::string(v) != "0";
   if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMallocHost(&I.h_io, 64) != cudaSuccess || cudaEventCreate(&I.ev0) != cudaSuccess ||
       cudaEventCreate(&I.ev1) != cudaSuccess) {

@@ -17,7 +17,7 @@ constexpr int N_EXPERT = 32;
 constexpr int N_USED = 4;
 constexpr int EXPERT_FF = 1792;
 constexpr int N_FF = 7168;
-constexpr int ATTN_SPLIT = 64;  // positions per decode-attention split
+constexpr int ATTN_SPLIT = 32;  // positions per decode-attention split (one per lane)
 
 // Activation source of a matvec: x, optionally RMS-normalised with `norm`
 // (kernels.rs:576-634 fused as a prologue).
@@ -66,6 +66,10 @@ void mv_lmhead(const Q6Mat& W, XSrc xs, float* logits, float2* partials, unsigne
 // Router logits + sigmoid top-4 (kernels.rs:552-574 + kernels/resident.rs:58-99).
 void router_top4(const float* Wr, const float* bias, XSrc xs, int* sel, float* selw,
                  const LaunchCfg& c);
+// Same over 32 CTAs (one expert logit each, last CTA selects); lg_scratch
+// holds 32 floats, counter one zeroed word.
+void router_top4_mc(const float* Wr, const float* bias, XSrc xs, float* lg_scratch, unsigned* counter, int* sel,
+                    float* selw, const LaunchCfg& c);
 // Embedding row dequant (kernels/resident.rs:4-18) for a device-resident token.
 void embed_token(const Q6Mat& E, const int* token, float* x, const LaunchCfg& c);
 // GQA decode attention: head RMSNorm + NEOX RoPE of q/k (kernels.rs:576-670),
@@ -79,13 +83,32 @@ struct AttnDecodeArgs {
   const int* pos;        // device position
   __half* kc;            // [8][ctx][64]
   __half* vc;            // [8][ctx][64]
-  float* part;           // [8][nsplit][4][66]
+  float* part;           // [8][nsplit][4][66], nsplit = ceil(ctx / ATTN_SPLIT)
   unsigned* counters;    // [8]
   float* out;            // a[2048]
   int ctx;
   float eps;
 };
 void attn_decode(const AttnDecodeArgs& a, const LaunchCfg& c);
+
+// TMA-staged variants (mvt.cu) for the engine's decode step: 1 CTA per SM,
+// bulk-copy weight pipeline issued before the PDL wait. `err` is the engine's
+// device error word (raised if a bounded mbarrier wait times out).
+bool mvt_supported(const Q6Mat& W);
+void mvt_plain(const Q6Mat& W, XSrc xs, float* y, unsigned* err, const LaunchCfg& c);
+void mvt_resid(const Q6Mat& W, XSrc xs, float* resid, unsigned* err, const LaunchCfg& c);
+// q, k, v projections in one launch: y = [q | k | v] (rows of 16-row tiles).
+void mvt_qkv(const Q6Mat& Wq, const Q6Mat& Wk, const Q6Mat& Wv, XSrc xs, float* y, unsigned* err,
+             const LaunchCfg& c);
+void mvt_conv(const Q6Mat& W, XSrc xs, const float* conv_w, float* state, float* gated, unsigned* err,
+              const LaunchCfg& c);
+void mvt_swiglu(const Q6Mat& Wg, const Q6Mat& Wu, XSrc xs, float* sw, unsigned* err, const LaunchCfg& c);
+void mvt_expert_swiglu(const Q6Mat& Wg, const Q6Mat& Wu, int ff, XSrc xs, const int* sel, float* sw, unsigned* err,
+                       const LaunchCfg& c);
+void mvt_expert_down(const Q6Mat& Wd, int ff, const float* sw, const int* sel, const float* selw, float* down,
+                     float* resid, unsigned* counter, unsigned* err, const LaunchCfg& c);
+void mvt_lmhead(const Q6Mat& W, XSrc xs, float* logits, float2* partials, unsigned* counter, int* token,
+                unsigned* err, const LaunchCfg& c);
 
 // ------------------------------------------------------------- generic ops
 void q6_dequant_rows(const Q6Mat& W, int row0, int nrows, float* out, cudaStream_t s);

@@ -70,7 +70,15 @@ lfm_status lfm_q6k_matmul(const void* w_dev, uint32_t in_dim, uint32_t rows, con
     return LFM_ERR_ARG;
   }
   lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
-  if (n == 1 && in_dim <= 2048) {
+  if (n == 1 && lfm::mvt_supported(W)) {
+    // the engine's TMA-staged decode matvec (no device error word here)
+    lfm::LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&c.sms, cudaDevAttrMultiProcessorCount, dev);
+    lfm::mvt_plain(W, lfm::XSrc{x_dev, nullptr, 0.f}, y_dev, nullptr, c);
+  } else if (n == 1 && in_dim <= 2048) {
     lfm::LaunchCfg c;
     c.stream = (cudaStream_t)stream;
     lfm::mv_plain(W, lfm::XSrc{x_dev, nullptr, 0.f}, y_dev, c);

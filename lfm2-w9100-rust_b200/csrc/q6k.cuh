@@ -109,30 +109,57 @@ __device__ __forceinline__ float sc_val(uint32_t scw, int m) {
   return (float)(int8_t)(uint8_t)(scw >> (8 * m));
 }
 
+// Packed fp32x2 arithmetic of sm_100 (two IEEE fp32 lanes per instruction,
+// same rounding as the scalar forms).
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rr;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rr, ra, rb;\n mov.b64 {%0, %1}, rr;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rc, rr;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rr, ra, rb, rc;\n mov.b64 {%0, %1}, rr;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+// Bytes j, j+1 of w as the exact floats (c - 32) (magic 2^23 mantissa trick).
+__device__ __forceinline__ float2 q6_val2(uint32_t w, int j) {
+  const float2 m = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)j)),
+                               __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)(j + 1))));
+  return f2_add(m, make_float2(-8388640.0f, -8388640.0f));
+}
+
 // Dot of one unit with the 64 activations x[m*16 + i] (element l0+i+32m of the
-// unit's half). Returns sum_m (d*sc_m) * sum_i (q6-32)*x.
+// unit's half). Returns sum_m (d*sc_m) * sum_i (q6-32)*x, with the inner sums
+// in fp32x2 pairs (even / odd i) added at the end.
 __device__ __forceinline__ float q6_unit_dot(const uint4& A, const uint4& B, const uint4& Q,
                                              uint32_t scw, float d, const float* x) {
   const uint32_t a[4] = {A.x, A.y, A.z, A.w};
   const uint32_t b[4] = {B.x, B.y, B.z, B.w};
   const uint32_t q[4] = {Q.x, Q.y, Q.z, Q.w};
-  float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+  const float2* x2 = reinterpret_cast<const float2*>(x);
+  float2 p0 = make_float2(0.f, 0.f), p1 = p0, p2 = p0, p3 = p0;
 #pragma unroll
   for (int t = 0; t < 4; t++) {
     uint32_t w0, w1, w2, w3;
     q6_words(a[t], b[t], q[t], w0, w1, w2, w3);
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      p0 = fmaf(q6_val(w0, j), x[0 * 16 + 4 * t + j], p0);
-      p1 = fmaf(q6_val(w1, j), x[1 * 16 + 4 * t + j], p1);
-      p2 = fmaf(q6_val(w2, j), x[2 * 16 + 4 * t + j], p2);
-      p3 = fmaf(q6_val(w3, j), x[3 * 16 + 4 * t + j], p3);
+    for (int j = 0; j < 4; j += 2) {
+      p0 = f2_fma(q6_val2(w0, j), x2[(0 * 16 + 4 * t + j) / 2], p0);
+      p1 = f2_fma(q6_val2(w1, j), x2[(1 * 16 + 4 * t + j) / 2], p1);
+      p2 = f2_fma(q6_val2(w2, j), x2[(2 * 16 + 4 * t + j) / 2], p2);
+      p3 = f2_fma(q6_val2(w3, j), x2[(3 * 16 + 4 * t + j) / 2], p3);
     }
   }
-  float r = (d * sc_val(scw, 0)) * p0;
-  r = fmaf(d * sc_val(scw, 1), p1, r);
-  r = fmaf(d * sc_val(scw, 2), p2, r);
-  r = fmaf(d * sc_val(scw, 3), p3, r);
+  float r = (d * sc_val(scw, 0)) * (p0.x + p0.y);
+  r = fmaf(d * sc_val(scw, 1), p1.x + p1.y, r);
+  r = fmaf(d * sc_val(scw, 2), p2.x + p2.y, r);
+  r = fmaf(d * sc_val(scw, 3), p3.x + p3.y, r);
   return r;
 }
 
