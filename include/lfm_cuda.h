@@ -180,6 +180,21 @@ lfm_status lfm_route(const float* logits_dev, const float* bias_dev, uint32_t n_
  * never wins. */
 lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream);
 
+/* lfm_argmax without any device allocation. It has no counterpart in the
+ * reference. lfm_argmax allocates 2 KiB of scratch per call with
+ * cudaMallocAsync; callers that may not allocate device memory at call time
+ * (a host that has handed the whole device to its own memory pool, or code
+ * running where the CUDA allocator must not be entered) call this instead.
+ * Its scratch is a fixed 2 KiB device array inside this library, present on
+ * every device that loads it until the process exits. Same result as
+ * lfm_argmax; n must be 1..2^30 (larger n returns LFM_ERR_ARG with a message
+ * in lfm_ops_error). The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture. All calls on a device share the one array: calls that overlap on
+ * the GPU (different streams, no ordering between them) race and may return
+ * wrong indices. */
+lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream);
+
 /* Message of the last failing kernel-level call on this thread. */
 const char* lfm_ops_error(void);
 

@@ -4,6 +4,7 @@
 // matvec microbench.
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -134,3 +135,74 @@ lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* s
 const char* lfm_ops_error(void) { return t_err.c_str(); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// lfm_argmax_noalloc: lfm_argmax with its scratch in a fixed device array.
+//
+// Some callers of this library cannot allocate device memory at call time: a
+// host that runs under a fixed memory budget and has already handed every byte
+// of the device to its own pool, an allocator that must not be re-entered from
+// inside its own callbacks, or a caller that may not touch the CUDA allocator
+// on that thread. lfm_argmax needs 2 KiB of scratch (one partial maximum per
+// CTA plus an arrival counter) and gets it with cudaMallocAsync; this variant
+// takes it from a file-scope device array instead, so it calls no allocating
+// routine at all.
+namespace {
+// The launcher (lfm::argmax_f32) runs at most 256 CTAs, each writing one
+// partial, so 256 slots suffice for every n. The kernel's grid-stride index is
+// a signed 32-bit int, so n is capped at 2^30 elements (4 GiB of fp32), well
+// clear of overflow.
+constexpr int kNoAllocPartials = 256;
+constexpr uint32_t kNoAllocMaxN = 1u << 30;
+
+// Slots 0..255: per-CTA partial maxima. Slot 256: its first word is the
+// last-CTA arrival counter, which must be 0 when the kernel starts.
+// One copy per device that loads this library (2 KiB + 8 B), held until the
+// process exits.
+static __device__ __align__(256) float2 g_argmax_scratch[kNoAllocPartials + 1];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float2* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_argmax_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, not a device address, so the
+// address is looked up once per device, with that device current, and cached.
+cudaError_t argmax_scratch(float2** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    float2* ptr = nullptr;
+    e = cudaGetSymbolAddress((void**)&ptr, g_argmax_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream) {
+  if (!x_dev || !out_dev || n == 0) {
+    t_err = "lfm_argmax_noalloc: bad argument";
+    return LFM_ERR_ARG;
+  }
+  if (n > kNoAllocMaxN) {
+    t_err = "lfm_argmax_noalloc: n = " + std::to_string(n) + " exceeds the maximum " +
+            std::to_string(kNoAllocMaxN) + " elements";
+    return LFM_ERR_ARG;
+  }
+  float2* sc = nullptr;
+  cudaError_t e = argmax_scratch(&sc);
+  if (e != cudaSuccess) return cuda_status(e);
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned* counter = (unsigned*)&sc[kNoAllocPartials];
+  // The array keeps whatever the previous call left: zero the counter first.
+  e = cudaMemsetAsync(counter, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return cuda_status(e);
+  lfm::argmax_f32(x_dev, (int)n, sc, counter, (int*)out_dev, s);
+  return cuda_status(cudaGetLastError());
+}
