@@ -117,6 +117,25 @@ lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_p
 /* CUDA-event device time (ms) of the last forward / decode call. */
 float lfm_last_device_ms(lfm_engine* e);
 
+/* Per-stage timeline of the persistent decode step, for profiling (the
+ * reference's per-dispatch GPU timestamp queries, vulkan/profile.rs:18-45,
+ * enabled by LFM_PROFILE_DISPATCH). `enable`
+ * switches %globaltimer stamps on for later decode steps; when `out` is
+ * non-null the last step's record is copied out as [n_stages][n_ctas][8]
+ * u64: stage start, activations staged, first weight tile ready, stage done
+ * (%globaltimer ns), then SM clock cycles waiting for weight tiles, tiles,
+ * cycles of tile compute, cycles of epilogues. n_stages = n_ctas = 0 when the
+ * kernel chain runs. */
+lfm_status lfm_step_trace(lfm_engine* e, int enable, uint64_t* out, size_t cap, uint32_t* n_stages,
+                          uint32_t* n_ctas);
+
+/* JSON description of the engine's decode path (persistent step or kernel
+ * chain, and why), SM count, resident weight bytes and launches per decode
+ * step (the reference reports its device and profile header at load,
+ * vulkan.rs:280-286, main.rs:198). The string stays valid until the next
+ * call on this engine. */
+const char* lfm_engine_info(lfm_engine* e);
+
 /* GpuEngine::reset_session (resident_graph.rs:105-115): zero the short-conv
  * state; stale KV beyond the valid prefix is never attended. */
 lfm_status lfm_reset_session(lfm_engine* e);

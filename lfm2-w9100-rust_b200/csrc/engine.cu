@@ -12,9 +12,11 @@
 //   * RoPE (cos, sin) table [ctx][32] computed once on the host with the same
 //     libm calls and operation order as the CPU path (lfm.rs:248-267).
 // A decode step (n == 1) is one CUDA graph: a 8-byte H2D copy of (token,
-// position), ~130 kernels chained with programmatic dependent launch, and a
-// 4-byte D2H copy of the argmax — the analogue of the reference's immutable
-// decode replay with a device-side position (vulkan/reusable.rs:4-173).
+// position), the step itself, and a 16-byte D2H copy of the argmax and the
+// status words — the analogue of the reference's immutable decode replay with
+// a device-side position (vulkan/reusable.rs:4-173). The step is a chain of
+// 126 kernels (mvt.cu / decode.cu), or, with LFM_STEP=1, one persistent
+// cooperative kernel (step.cu) when it fits one CTA per SM.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <string.h>
@@ -29,6 +31,7 @@
 #include "../../include/lfm_cuda.h"
 #include "gguf.h"
 #include "kernels.h"
+#include "step.h"
 
 namespace lfm {
 
@@ -79,6 +82,15 @@ struct EngineImpl {
   bool pdl = false;  // programmatic dependent launch between decode kernels (LFM_PDL=1)
   bool use_graph = true;
   bool use_mvt = true;  // TMA-staged decode matvecs
+  bool use_step = false;  // persistent decode step (LFM_STEP=1); the kernel chain is faster today
+  std::string step_reason;  // why the persistent step is not in use
+  StepCtl* ctl = nullptr;
+  StepStage* d_stages = nullptr;
+  int nstages = 0;
+  unsigned long long* trace = nullptr;  // [stage][cta][4] globaltimer stamps
+  bool trace_on = false;
+  uint64_t step_epochs = 0;  // steps since the control block was zeroed
+  std::string info;
 
   // resident state
   uint32_t ctx = 4096;
@@ -138,6 +150,9 @@ struct EngineImpl {
     for (void* p : state_allocs) cudaFree(p);
     state_allocs.clear();
     state_ready = false;
+    ctl = nullptr;
+    d_stages = nullptr;
+    trace = nullptr;
     if (graph) {
       cudaGraphExecDestroy(graph);
       graph = nullptr;
@@ -162,6 +177,10 @@ struct EngineImpl {
   // --------------------------------------------------------------- state
   void ensure_state();
   void ensure_prefill(int n);
+  void build_step();
+  bool step_active() const { return use_step && ctl != nullptr; }
+  void drop_graphs();
+  void step_epoch_guard(uint64_t steps);
 
   // ------------------------------------------------------------- forward
   void enqueue_decode(cudaStream_t s, bool pdl_on);
@@ -387,9 +406,109 @@ void EngineImpl::ensure_state() {
   counters = dalloc<unsigned>(state_allocs, 1024);
   CK(cudaMemsetAsync(counters, 0, 1024 * 4, stream));
   am_part = dalloc<float2>(state_allocs, 4096);
+  ctl = nullptr;
+  d_stages = nullptr;
+  trace = nullptr;
+  if (use_step) build_step();
   CK(cudaStreamSynchronize(stream));
   state_ready = true;
   state_ctx = ctx;
+}
+
+// The step's barrier counters grow by one grid per step; zero the control
+// block long before they could wrap (2^32 / 148 steps), between launches.
+void EngineImpl::step_epoch_guard(uint64_t steps) {
+  if (!step_active()) return;
+  if (step_epochs + steps > (1ull << 24)) {
+    CK(cudaMemsetAsync(ctl, 0, sizeof(StepCtl), stream));
+    step_epochs = 0;
+  }
+  step_epochs += steps;
+}
+
+void EngineImpl::drop_graphs() {
+  if (graph) {
+    cudaGraphExecDestroy(graph);
+    graph = nullptr;
+  }
+  if (loop_graph) {
+    cudaGraphExecDestroy(loop_graph);
+    loop_graph = nullptr;
+  }
+}
+
+// Stage list of the persistent decode step: the reference's resident decode
+// graph (resident_graph.rs:226-546) in dependency order.
+void EngineImpl::build_step() {
+  cudaError_t e = step_prepare();
+  if (e != cudaSuccess) {
+    step_reason = std::string("persistent step unavailable: ") + cudaGetErrorString(e) + " (" +
+                  step_occupancy_report() + ")";
+    cudaGetLastError();
+    return;
+  }
+  if (sms > STEP_MAX_CTAS) {
+    step_reason = "persistent step unavailable: more SMs than the control block holds";
+    return;
+  }
+  std::vector<StepStage> st;
+  auto add = [&](int type) -> StepStage& {
+    st.push_back(StepStage{});
+    st.back().type = type;
+    return st.back();
+  };
+  add(ST_EMBED);
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const LayerW& L = layers[l];
+    if (L.attn) {
+      StepStage& q = add(ST_QKV);
+      q.W = L.q, q.W2 = L.k, q.W3 = L.v;
+      q.xin = x, q.norm = L.attn_norm, q.out = qkv;
+      q.ntiles = (L.q.rows + L.k.rows + L.v.rows) / 16;
+      StepStage& at = add(ST_ATTN);
+      at.xin = qkv, at.q_norm = L.q_norm, at.k_norm = L.k_norm, at.out = a;
+      at.kc = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      at.vc = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      StepStage& o = add(ST_RESID);
+      o.W = L.o, o.xin = a, o.resid = x, o.ntiles = L.o.rows / 16;
+    } else {
+      StepStage& c = add(ST_CONV);
+      c.W = L.in_proj, c.xin = x, c.norm = L.attn_norm, c.conv_w = L.conv_w;
+      c.state = conv_state + (size_t)L.conv_idx * DIM * 2, c.out = gated, c.ntiles = DIM / 8;
+      StepStage& o = add(ST_RESID);
+      o.W = L.out_proj, o.xin = gated, o.resid = x, o.ntiles = L.out_proj.rows / 16;
+    }
+    if (L.dense) {
+      StepStage& g = add(ST_SWIGLU);
+      g.W = L.gate, g.W2 = L.up, g.xin = x, g.norm = L.ffn_norm, g.out = sw, g.ntiles = L.gate.rows / 8;
+      StepStage& d = add(ST_DOWN28);
+      d.W = L.down, d.xin = sw, d.resid = x, d.ntiles = L.down.rows / 4;
+    } else {
+      const int dep = (int)st.size();
+      StepStage& r = add(ST_ROUTER);
+      r.rw = L.router, r.bias = L.bias, r.xin = x, r.norm = L.ffn_norm;
+      StepStage& g = add(ST_XSWIGLU);
+      g.W = L.gate_x, g.W2 = L.up_x, g.xin = x, g.norm = L.ffn_norm, g.out = sw, g.ff = EXPERT_FF;
+      g.ntiles = N_USED * EXPERT_FF / 8, g.dep = dep;
+      StepStage& d = add(ST_XDOWN);
+      d.W = L.down_x, d.xin = sw, d.resid = x, d.ff = EXPERT_FF, d.ntiles = DIM / 4, d.dep = dep;
+    }
+  }
+  StepStage& h = add(ST_LMHEAD);
+  h.W = embd, h.xin = x, h.norm = out_norm, h.out = logits, h.ntiles = embd.rows / 16;
+  if ((int)st.size() > STEP_MAX_STAGES || embd.rows % 16 != 0) {
+    step_reason = "persistent step unavailable: model shape outside the step kernel's tiling";
+    return;
+  }
+  nstages = (int)st.size();
+  d_stages = dalloc<StepStage>(state_allocs, st.size());
+  CK(cudaMemcpy(d_stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice));
+  ctl = dalloc<StepCtl>(state_allocs, 1);
+  CK(cudaMemsetAsync(ctl, 0, sizeof(StepCtl), stream));
+  step_epochs = 0;
+  trace = dalloc<unsigned long long>(state_allocs, (size_t)STEP_MAX_STAGES * STEP_MAX_CTAS * STEP_TRACE_FIELDS);
+  CK(cudaMemsetAsync(trace, 0, (size_t)STEP_MAX_STAGES * STEP_MAX_CTAS * STEP_TRACE_FIELDS * 8, stream));
+  step_reason.clear();
 }
 
 void EngineImpl::ensure_prefill(int n) {
@@ -425,6 +544,23 @@ void EngineImpl::enqueue_decode(cudaStream_t s, bool pdl_on) {
   int n = 0;
   const float eps = hp.eps;
   unsigned* err = (unsigned*)(io + 4);
+  if (step_active()) {
+    StepParams p = {};
+    p.stages = d_stages;
+    p.nstages = nstages;
+    p.ctl = ctl;
+    p.io = io;
+    p.rope = rope;
+    p.attn_part = attn_part;
+    p.ctx = (int)ctx;
+    p.eps = eps;
+    p.embd = embd;
+    p.x = x;
+    p.trace = trace_on ? trace : nullptr;
+    CK(step_launch(p, sms, s));
+    launches_per_decode = 1;
+    return;
+  }
   embed_token(embd, io + 0, x, c);
   n++;
   for (uint32_t l = 0; l < hp.n_layers; l++) {
@@ -499,6 +635,7 @@ void EngineImpl::enqueue_ffn(const LayerW& L, float* xr, const LaunchCfg& c, uns
 void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
   h_io[0] = (int)token;
   h_io[1] = (int)pos;
+  step_epoch_guard(1);
   CK(cudaEventRecord(ev0, stream));
   if (use_graph) {
     if (!graph) {
@@ -507,6 +644,7 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
       cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream);
       enqueue_decode(stream, pdl);
       cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, stream);
+      if (step_active()) cudaMemcpyAsync(h_io + 5, &ctl->err, 4, cudaMemcpyDeviceToHost, stream);
       CK(cudaStreamEndCapture(stream, &g));
       cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
       cudaGraphDestroy(g);
@@ -520,6 +658,7 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
     CK(cudaMemcpyAsync(io, h_io, 8, cudaMemcpyHostToDevice, stream));
     enqueue_decode(stream, pdl);
     CK(cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, stream));
+    if (step_active()) CK(cudaMemcpyAsync(h_io + 5, &ctl->err, 4, cudaMemcpyDeviceToHost, stream));
   }
   CK(cudaEventRecord(ev1, stream));
   CK(cudaStreamSynchronize(stream));
@@ -530,13 +669,20 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
   check_device_error();
 }
 
-// The device error word (io[4]) is raised by a bounded wait that timed out.
+// The device status words (io[4] for the kernel chain, ctl->err for the
+// persistent step) are raised by a bounded wait that timed out. After a
+// timeout the step's barrier counters are inconsistent, so the control block
+// is zeroed (epoch 0) before the next step.
 void EngineImpl::check_device_error() {
-  if (h_io[4] != 0) {
-    h_io[4] = 0;
+  const int chain = h_io[4], step = h_io[5];
+  if (chain != 0 || step != 0) {
+    h_io[4] = h_io[5] = 0;
     cudaMemsetAsync(io + 4, 0, 4, stream);
+    if (ctl) cudaMemsetAsync(ctl, 0, sizeof(StepCtl), stream);
+    step_epochs = 0;
     cudaStreamSynchronize(stream);
-    throw std::runtime_error("device status word raised: a bounded wait in a kernel timed out");
+    throw std::runtime_error(std::string("device status word raised (") + (step ? "persistent step" : "kernel chain") +
+                             " code " + std::to_string(step ? step : chain) + "): a bounded wait in a kernel timed out");
   }
 }
 
@@ -580,11 +726,13 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
   }
   // io[0..2] hold the last decode step (token, position, next); io[3] = 0.
   CK(cudaMemsetAsync(io + 3, 0, 4, stream));
+  step_epoch_guard(steps);
   CK(cudaEventRecord(ev0, stream));
   for (uint32_t i = 0; i < steps; i++) CK(cudaGraphLaunch(loop_graph, stream));
   CK(cudaEventRecord(ev1, stream));
   CK(cudaMemcpyAsync(out_tokens, loop_tokens, (size_t)steps * 4, cudaMemcpyDeviceToHost, stream));
   CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, stream));
+  if (step_active()) CK(cudaMemcpyAsync(h_io + 5, &ctl->err, 4, cudaMemcpyDeviceToHost, stream));
   CK(cudaStreamSynchronize(stream));
   CK(cudaGetLastError());
   CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
@@ -824,6 +972,8 @@ lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out
   if (const char* v = getenv("LFM_PDL")) I.pdl = std::string(v) != "0";
   if (const char* v = getenv("LFM_GRAPH")) I.use_graph = std::string(v) != "0";
   if (const char* v = getenv("LFM_MVT")) I.use_mvt = std::string(v) != "0";
+  if (const char* v = getenv("LFM_STEP")) I.use_step = std::string(v) != "0";
+  if (!I.use_step) I.step_reason = "persistent step not selected (LFM_STEP=1 selects it)";
   if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMallocHost(&I.h_io, 64) != cudaSuccess || cudaEventCreate(&I.ev0) != cudaSuccess ||
       cudaEventCreate(&I.ev1) != cudaSuccess) {
@@ -943,6 +1093,48 @@ lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_p
 }
 
 float lfm_last_device_ms(lfm_engine* e) { return e ? e->impl.last_ms : 0.f; }
+
+lfm_status lfm_step_trace(lfm_engine* e, int enable, uint64_t* out, size_t cap, uint32_t* n_stages,
+                          uint32_t* n_ctas) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    I.ensure_state();
+    if (n_stages) *n_stages = I.step_active() ? (uint32_t)I.nstages : 0;
+    if (n_ctas) *n_ctas = I.step_active() ? (uint32_t)I.sms : 0;
+    if (out && I.step_active()) {
+      const size_t need = (size_t)I.nstages * I.sms * lfm::STEP_TRACE_FIELDS;
+      if (cap < need) {
+        lfm::set_err(&I, "trace buffer too small");
+        return LFM_ERR_ARG;
+      }
+      std::vector<unsigned long long> all((size_t)lfm::STEP_MAX_STAGES * lfm::STEP_MAX_CTAS * lfm::STEP_TRACE_FIELDS);
+      CK(cudaMemcpy(all.data(), I.trace, need * 8, cudaMemcpyDeviceToHost));
+      memcpy(out, all.data(), need * 8);
+    }
+    const bool on = enable != 0;
+    if (on != I.trace_on) {
+      I.trace_on = on;
+      I.drop_graphs();  // the captured launches carry the trace pointer
+    }
+    return LFM_OK;
+  });
+}
+
+const char* lfm_engine_info(lfm_engine* e) {
+  if (!e) return "{}";
+  EngineImpl& I = e->impl;
+  std::string path = I.step_active() ? "persistent-step" : (I.use_mvt ? "kernel-chain-tma" : "kernel-chain-simt");
+  if (!I.state_ready) path = I.use_step ? "persistent-step (pending first decode)" : path;
+  std::string reason = I.step_reason;
+  for (char& ch : reason)
+    if (ch == '"' || ch == '\\') ch = '\'';
+  I.info = "{\"decode_path\": \"" + path + "\", \"step_reason\": \"" + reason + "\", \"sms\": " +
+           std::to_string(I.sms) + ", \"weight_bytes\": " + std::to_string(I.weight_bytes) + ", \"pdl\": " +
+           (I.pdl ? "true" : "false") + ", \"graph\": " + (I.use_graph ? "true" : "false") +
+           ", \"step_stages\": " + std::to_string(I.nstages) + ", \"launches_per_decode\": " +
+           std::to_string(I.launches_per_decode) + "}";
+  return I.info.c_str();
+}
 
 lfm_status lfm_reset_session(lfm_engine* e) {
   return guarded(e, [&]() -> lfm_status {

@@ -21,7 +21,7 @@
 
 #include <stdlib.h>
 
-#include "kernels.h"
+#include "dev_common.cuh"
 
 namespace lfm {
 namespace {
@@ -49,65 +49,7 @@ struct MvtParams {
   Q6Mat W3;       // M_QKV: W = q, W2 = k, W3 = v (outputs y, y + q.rows, ...)
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-// try_wait with a suspend-time hint: the thread sleeps in hardware until the
-// phase completes or ~10 us pass, instead of spinning on the issue slots.
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity), "r"(10000u)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t gtime() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait: false after ~1 s without completion (error word raised).
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, unsigned* err) {
-  if (mbar_try_wait(b, parity)) return true;
-  const uint64_t t0 = gtime();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait(b, parity)) return true;
-    if ((i & 255u) == 0 && gtime() - t0 > 1000000000ull) {
-      if (err) atomicExch(err, 1u);
-      return false;
-    }
-  }
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
-  return v > bv || (v == bv && i < bi);
-}
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+using namespace dev;
 
 template <int MODE>
 struct TileDef {
@@ -451,14 +393,17 @@ void launch_mvt(const MvtParams& p, const LaunchCfg& c) {
     cudaFuncSetAttribute(k_mvt<MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
-  // one or two CTAs per SM (two hide more dependent-instruction latency;
-  // each CTA keeps its own 3-4 stage weight ring)
-  static int per_sm = 0;
-  if (per_sm == 0) {
+  // One or two CTAs per SM. Two hide more dependent-instruction latency (each
+  // CTA keeps its own 3-4 stage weight ring) and pay off when every CTA has
+  // many tiles (lm_head); for the short per-layer matrices one CTA per SM
+  // measured faster (fewer ring fills per tile).
+  static int env_per_sm = -1;
+  if (env_per_sm < 0) {
     const char* v = getenv("LFM_MVT_CTAS_PER_SM");
-    per_sm = v ? atoi(v) : 2;
-    if (per_sm < 1 || per_sm > 2) per_sm = 2;
+    env_per_sm = v ? atoi(v) : 0;
+    if (env_per_sm < 0 || env_per_sm > 2) env_per_sm = 0;
   }
+  const int per_sm = env_per_sm ? env_per_sm : (p.ntiles >= 16 * c.sms ? 2 : 1);
   const int cap = c.sms * per_sm;
   int g = p.ntiles < cap ? p.ntiles : cap;
   if (g < 1) g = 1;

@@ -45,6 +45,7 @@ _lib = None
 EXPORTS = [
     "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
     "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
+    "lfm_step_trace", "lfm_engine_info",
     "lfm_reset_session",
     "lfm_snapshot_cache", "lfm_restore_cache", "lfm_snapshot_logits", "lfm_counters_get",
     "lfm_device_name", "lfm_last_error", "lfm_global_error", "lfm_q6k_device_bytes",
@@ -73,6 +74,8 @@ def lib() -> ctypes.CDLL:
         "lfm_generate": ([P, P, U32, U32, U32, P, ctypes.POINTER(U32)], st),
         "lfm_decode_loop": ([P, U32, U32, U32, P, ctypes.POINTER(ctypes.c_float)], st),
         "lfm_last_device_ms": ([P], ctypes.c_float),
+        "lfm_step_trace": ([P, ctypes.c_int, P, SZ, ctypes.POINTER(U32), ctypes.POINTER(U32)], st),
+        "lfm_engine_info": ([P], ctypes.c_char_p),
         "lfm_reset_session": ([P], st),
         "lfm_snapshot_cache": ([P, U32, P, SZ, ctypes.POINTER(SZ)], st),
         "lfm_restore_cache": ([P, U32, P, SZ], st),
@@ -176,6 +179,25 @@ class GpuEngine:
 
     def last_device_ms(self) -> float:
         return float(lib().lfm_last_device_ms(self.h))
+
+    def step_trace(self, enable: bool):
+        """Switch per-stage timestamps of the persistent decode step on/off and
+        return the last step's record as uint64 [stages][ctas][8] (None when
+        the kernel chain runs): start, staged, first tile, done (ns stamps),
+        tile wait cycles, tiles, tile compute cycles, epilogue cycles."""
+        ns, nc = ctypes.c_uint32(), ctypes.c_uint32()
+        self._check(lib().lfm_step_trace(self.h, 1 if enable else 0, None, 0, ctypes.byref(ns), ctypes.byref(nc)),
+                    "step_trace")
+        if ns.value == 0:
+            return None
+        out = np.zeros((ns.value, nc.value, 8), dtype=np.uint64)
+        self._check(lib().lfm_step_trace(self.h, 1 if enable else 0, _p(out), out.size, None, None), "step_trace")
+        return out
+
+    def info(self) -> dict:
+        """Decode path and launch facts of this engine (JSON from the library)."""
+        import json
+        return json.loads(lib().lfm_engine_info(self.h).decode())
 
     def reset_session(self):
         self._check(lib().lfm_reset_session(self.h), "reset_session")
