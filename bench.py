@@ -38,6 +38,9 @@ METRIC = "decode tok/s bs1 @512 ctx; prefill tok/s @3840; % of HBM/tensor roofli
 PROMPT_LEN = 512
 PREFILL_LEN = 3840
 SEED = 1234
+# DRAM bytes (read + write) of one decode step from an ncu capture of the same
+# workload (profiles/ holds the capture summary); keyed by decode path.
+TRAFFIC: dict = {"persistent-step": 1442.7e6}
 DIM, VOCAB = 2048, 128000
 N_ATTN, N_CONV, N_DENSE, N_MOE = 6, 18, 2, 22
 
@@ -347,9 +350,13 @@ def main():
     avg_ctx = PROMPT_LEN + 1 + (args.steps + 1) / 2.0
     bpt = decode_bytes_per_token(avg_ctx)
     achieved = bpt["total"] * per_gpu / 1e9
+    info = eng.info()
+    path_name = info["decode_path"]
+    kernel = ("k_step: one persistent cooperative kernel per decode token" if path_name == "persistent-step"
+              else f"decode step as a CUDA graph of {info['launches_per_decode']} kernels")
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
-                "kernel": "decode step (one CUDA graph per token)", "bytes_per_step": int(bpt["total"]),
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": TRAFFIC.get(path_name),
+                "kernel": kernel, "bytes_per_step": int(bpt["total"]),
                 "peak_source": peaks["source"]}
 
     prefill = None
@@ -380,6 +387,7 @@ def main():
                 "data": "synthetic seeded random-init Q6_K weights of the exact architecture",
                 "config": {"workload": "config 2: 512-token seeded prompt, greedy bs1 decode",
                            "prompt_len": PROMPT_LEN, "ctx": 4096, "parallelism": f"replicas x{ws}",
+                           "decode_path": path_name,
                            "l2": "no flush needed: every step streams ~1.4 GB of weights (> 126 MB L2)"},
                 "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "prefill": prefill, "microbench": micro, "cpu_baseline": cpu,

@@ -580,11 +580,17 @@ __global__ void k_route_n(const float* logits, const float* bias, int n_expert, 
 }
 
 // Embedding: one warp dequantises row `tok` (32 units of 64 weights).
-__global__ void k_embed(Q6Mat E, const int* token, float* x) {
+__global__ void k_embed(Q6Mat E, const int* token, float* x, unsigned* err) {
   pdl_trigger();
   pdl_wait();
-  const int tok = *token;
+  int tok = *token;
   const int u = threadIdx.x;
+  // the id comes from device memory (the previous step's argmax): a value
+  // outside the table raises the status word and reads row 0 instead
+  if ((unsigned)tok >= (unsigned)E.rows) {
+    if (u == 0 && err) atomicExch(err, 4u);
+    tok = 0;
+  }
   const int U = 4 * E.nb;
   if (u >= U) return;
   const uint4* qp = E.q + (size_t)tok * 3 * U + u;
@@ -754,8 +760,8 @@ void route_n(const float* logits, const float* bias, int n_expert, int n, int* s
   k_route_n<<<(n + 7) / 8, 256, 0, s>>>(logits, bias, n_expert, n, sel, selw);
 }
 
-void embed_token(const Q6Mat& E, const int* token, float* x, const LaunchCfg& c) {
-  launch_pdl(k_embed, dim3(1), dim3(32), c, E, token, x);
+void embed_token(const Q6Mat& E, const int* token, float* x, unsigned* err, const LaunchCfg& c) {
+  launch_pdl(k_embed, dim3(1), dim3(32), c, E, token, x, err);
 }
 
 void attn_decode(const AttnDecodeArgs& a, const LaunchCfg& c) {

@@ -14,9 +14,9 @@
 // A decode step (n == 1) is one CUDA graph: a 8-byte H2D copy of (token,
 // position), the step itself, and a 16-byte D2H copy of the argmax and the
 // status words — the analogue of the reference's immutable decode replay with
-// a device-side position (vulkan/reusable.rs:4-173). The step is a chain of
-// 126 kernels (mvt.cu / decode.cu), or, with LFM_STEP=1, one persistent
-// cooperative kernel (step.cu) when it fits one CTA per SM.
+// a device-side position (vulkan/reusable.rs:4-173). The step is one
+// persistent cooperative kernel (step.cu) when it fits one CTA per SM, else
+// (or with LFM_STEP=0) a chain of 126 kernels (mvt.cu / decode.cu).
 #include <cuda_runtime.h>
 #include <math.h>
 #include <string.h>
@@ -82,7 +82,7 @@ struct EngineImpl {
   bool pdl = false;  // programmatic dependent launch between decode kernels (LFM_PDL=1)
   bool use_graph = true;
   bool use_mvt = true;  // TMA-staged decode matvecs
-  bool use_step = false;  // persistent decode step (LFM_STEP=1); the kernel chain is faster today
+  bool use_step = true;  // persistent decode step (LFM_STEP=0 selects the kernel chain)
   std::string step_reason;  // why the persistent step is not in use
   StepCtl* ctl = nullptr;
   StepStage* d_stages = nullptr;
@@ -496,6 +496,14 @@ void EngineImpl::build_step() {
   }
   StepStage& h = add(ST_LMHEAD);
   h.W = embd, h.xin = x, h.norm = out_norm, h.out = logits, h.ntiles = embd.rows / 16;
+  for (const StepStage& q : st) {
+    const bool partial = q.type == ST_CONV || q.type == ST_SWIGLU || q.type == ST_XSWIGLU || q.type == ST_XDOWN ||
+                         q.type == ST_DOWN28;
+    if (partial && (q.ntiles + sms - 1) / sms > STEP_PART_TILES) {
+      step_reason = "persistent step unavailable: too few SMs for the per-CTA partial buffer";
+      return;
+    }
+  }
   if ((int)st.size() > STEP_MAX_STAGES || embd.rows % 16 != 0) {
     step_reason = "persistent step unavailable: model shape outside the step kernel's tiling";
     return;
@@ -561,7 +569,7 @@ void EngineImpl::enqueue_decode(cudaStream_t s, bool pdl_on) {
     launches_per_decode = 1;
     return;
   }
-  embed_token(embd, io + 0, x, c);
+  embed_token(embd, io + 0, x, err, c);
   n++;
   for (uint32_t l = 0; l < hp.n_layers; l++) {
     const LayerW& L = layers[l];
@@ -670,7 +678,8 @@ void EngineImpl::run_decode(uint32_t token, uint32_t pos) {
 }
 
 // The device status words (io[4] for the kernel chain, ctl->err for the
-// persistent step) are raised by a bounded wait that timed out. After a
+// persistent step) are raised by a bounded wait that timed out (codes 1-3) or
+// by an embedding lookup of an out-of-range device-side token id (4). After a
 // timeout the step's barrier counters are inconsistent, so the control block
 // is zeroed (epoch 0) before the next step.
 void EngineImpl::check_device_error() {
@@ -681,8 +690,11 @@ void EngineImpl::check_device_error() {
     if (ctl) cudaMemsetAsync(ctl, 0, sizeof(StepCtl), stream);
     step_epochs = 0;
     cudaStreamSynchronize(stream);
+    const int code = step ? step : chain;
     throw std::runtime_error(std::string("device status word raised (") + (step ? "persistent step" : "kernel chain") +
-                             " code " + std::to_string(step ? step : chain) + "): a bounded wait in a kernel timed out");
+                             " code " + std::to_string(code) + "): " +
+                             (code == 4 ? "a device-side token id was outside the vocabulary"
+                                        : "a bounded wait in a kernel timed out"));
   }
 }
 
@@ -973,7 +985,7 @@ lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out
   if (const char* v = getenv("LFM_GRAPH")) I.use_graph = std::string(v) != "0";
   if (const char* v = getenv("LFM_MVT")) I.use_mvt = std::string(v) != "0";
   if (const char* v = getenv("LFM_STEP")) I.use_step = std::string(v) != "0";
-  if (!I.use_step) I.step_reason = "persistent step not selected (LFM_STEP=1 selects it)";
+  if (!I.use_step) I.step_reason = "persistent step disabled (LFM_STEP=0)";
   if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMallocHost(&I.h_io, 64) != cudaSuccess || cudaEventCreate(&I.ev0) != cudaSuccess ||
       cudaEventCreate(&I.ev1) != cudaSuccess) {

@@ -70,8 +70,9 @@ void router_top4(const float* Wr, const float* bias, XSrc xs, int* sel, float* s
 // holds 32 floats, counter one zeroed word.
 void router_top4_mc(const float* Wr, const float* bias, XSrc xs, float* lg_scratch, unsigned* counter, int* sel,
                     float* selw, const LaunchCfg& c);
-// Embedding row dequant (kernels/resident.rs:4-18) for a device-resident token.
-void embed_token(const Q6Mat& E, const int* token, float* x, const LaunchCfg& c);
+// Embedding row dequant (kernels/resident.rs:4-18) for a device-resident token;
+// an id outside the table raises *err (code 4) and reads row 0.
+void embed_token(const Q6Mat& E, const int* token, float* x, unsigned* err, const LaunchCfg& c);
 // GQA decode attention: head RMSNorm + NEOX RoPE of q/k (kernels.rs:576-670),
 // fp16 KV write at *pos (kernels/resident.rs:119-169), split attention and
 // merge (kernels/attention_split.rs:3-33).

@@ -5,25 +5,29 @@
 // (gpu_lfm/resident_graph.rs:226-546) become a stage list walked in order by
 // every CTA. Between dependent stages the CTAs meet at a grid barrier
 // (monotonic arrival counters in global memory, acquire/release ordering,
-// bounded polling). Thread 0 of each CTA doubles as the producer: a
-// non-blocking state machine, advanced whenever thread 0 would otherwise wait,
-// streams this CTA's weight tiles of ALL stages, in order, through a 4-slot
-// shared-memory ring with bulk async copies (cp.async.bulk, no multicast)
-// completed on mbarriers. It waits on no grid barrier except before
-// routed-expert tiles (the expert ids come from the router stage), so the
-// weight stream of stage s+1.. is in flight while stage s computes, and HBM
-// streaming continues across the dependency chain instead of restarting at
-// every kernel boundary. (A separate producer warp would make 17 warps, and
-// the register file is split over four SM sub-partitions: 17 warps cap every
-// thread at 96 registers, 16 warps allow 128.)
+// bounded polling).
 //
-// All 16 warps compute: they hold the stage's activation vector in registers
-// (one 64-weight unit per lane, q6k.cuh layout), dequantise weight tiles from
-// the ring, and run the stage epilogues (residual, short conv, SwiGLU,
-// rank-ordered expert combine, argmax). Activations written by other CTAs are
-// read with L2-coherent loads (ld.global.cg). Every wait is bounded (1 s); a
-// timeout raises the status word, sets an abort flag that releases all other
-// waits, and the kernel drains its copies and returns.
+// Warp 8 of each CTA is a dedicated producer: it walks this CTA's weight
+// tiles of ALL stages in order and streams them through a 4-slot
+// shared-memory ring with bulk async copies (cp.async.bulk, no multicast)
+// completed on mbarriers. It waits only for free ring slots and, before
+// routed-expert tiles, for the router stage (the expert ids), so the weight
+// stream of later stages is in flight while earlier stages compute and the
+// grid barriers never drain the HBM pipeline.
+//
+// Warps 0-15 consume. Each holds the stage's activation unit in registers (one
+// 64-weight unit per lane, q6k.cuh layout) and computes one dot row of every
+// tile on its own: wait for the tile, dequantise and reduce, release the slot,
+// and either finish the row (projection output, residual add, logits and
+// argmax) or park the dot in a shared-memory partial buffer, with no CTA-wide
+// barrier per tile. Rows that combine several dots (short conv b/c/x, SwiGLU
+// gate/up, the rank-ordered expert combine, the dense down projection split in
+// quarters) are finished at the end of the stage by the CTA that owns them.
+//
+// Every wait is bounded (~1 s of SM cycles). A timeout raises the status word
+// and an abort flag that releases all other waits; the consumers agree on it
+// at the next stage boundary, the producer drains its copies, and the kernel
+// returns.
 #include <math.h>
 
 #include <string>
@@ -35,8 +39,11 @@ namespace lfm {
 namespace {
 using namespace dev;
 
-constexpr int NCW = 16;                // warps; all compute, thread 0 also produces
-constexpr int NT = NCW * 32;           // 16 warps x 128 registers fill the register file
+constexpr int NCW = 16;                // consumer warps
+constexpr int NT = (NCW + 1) * 32;     // + the producer warp
+constexpr int MAXREG = 96;             // 17 warps: 5 on one SM sub-partition x 96 registers
+constexpr int PART_TILES = STEP_PART_TILES;
+constexpr int PRODUCER = NCW;          // warp index of the producer
 constexpr int RING = 4;
 constexpr int SLOT = 40320;            // 24 rows x (1536 + 128 + 16): the largest tile
 constexpr int KP = HEAD_DIM + 8;       // padded fp16 K row in shared memory
@@ -75,14 +82,23 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
   return v;
 }
 __device__ __forceinline__ unsigned ld_vol(const unsigned* p) { return *(volatile const unsigned*)p; }
-// Stage descriptors live in shared memory, after the weight ring: an acquire
-// at gpu scope invalidates L1, so descriptors read from global memory would
-// turn every producer step into a chain of L2 round trips.
-__device__ __forceinline__ StepStage* stage_table(uint8_t* ring) { return (StepStage*)(ring + RING * SLOT); }
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
-// CTA barriers in the non-aligned form: thread 0 may reach them from its own
-// producer/poll path while the rest of warp 0 is already waiting.
+// Stage descriptors live in shared memory, after the weight ring.
+__device__ __forceinline__ StepStage* stage_table(uint8_t* ring) { return (StepStage*)(ring + RING * SLOT); }
+
+// Barriers among the 256 consumer threads (named barrier 1; the producer warp
+// never takes part). Non-aligned form: thread 0 reaches it from its own poll.
 __device__ __forceinline__ void cons_sync() { asm volatile("barrier.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
+// ... and the same barrier reducing a predicate: true if any consumer passed true
+__device__ __forceinline__ bool cons_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n barrier.red.or.pred po, 1, %2, pi;\n selp.u32 %0, 1, 0, po;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(NCW * 32)
+      : "memory");
+  return r != 0;
+}
 // named barriers 2..3: the two 4-warp attention groups
 __device__ __forceinline__ void group_sync(int g) {
   if (g == 0)
@@ -105,6 +121,22 @@ __device__ bool ring_wait(uint64_t* b, uint32_t parity, StepCtl* ctl) {
       if (ld_vol(&ctl->abort)) return false;
       if (wb.spent()) {
         raise_abort(ctl, 3u);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for a grid barrier counter (relaxed polls, one acquire once
+// reached: an acquire at gpu scope invalidates L1).
+__device__ bool counter_wait(const unsigned* c, unsigned target, StepCtl* ctl, unsigned code) {
+  WaitBudget wb;
+  for (uint32_t i = 0;; i++) {
+    if (ld_relaxed(c) >= target && ld_acquire(c) >= target) return true;
+    if ((i & 15u) == 15u) {
+      if (ld_vol(&ctl->abort)) return false;
+      if (wb.spent()) {
+        raise_abort(ctl, code);
         return false;
       }
     }
@@ -171,34 +203,8 @@ __device__ __forceinline__ void tile_range(int ntiles, int& t0, int& t1) {
 }
 
 // --------------------------------------------------------------- producer
-// Thread 0 is also the producer: a non-blocking state machine walks this CTA's
-// weight tiles of all stages in order and issues each one as soon as its ring
-// slot is free (and, for expert tiles, once the router stage has published the
-// expert ids). Thread 0 advances it whenever it would otherwise wait. Its state
-// lives in shared memory between polls; a poll copies it and the stage fields
-// it needs into registers first, because every mbarrier / bulk-copy asm
-// statement is a compiler memory barrier that would otherwise turn each field
-// access into a fresh shared-memory round trip on the critical path.
-struct Cursor {
-  int s, t, t1, k;  // stage, tile, end tile, tiles issued so far
-  int ready;        // tile range (and expert ids) of stage s loaded
-  int sel[N_USED];
-};
-
-__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // Producer-side forms of the mbarrier / bulk-copy instructions without a
-// compiler memory clobber: the producer reads no data that these order (the
-// consumers' view of a tile is ordered by their own waits on the full
-// barrier), so the compiler may keep descriptor fields in registers across them.
+// compiler memory clobber: the producer reads nothing these order.
 __device__ __forceinline__ void p_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes));
 }
@@ -207,23 +213,14 @@ __device__ __forceinline__ void p_bulk(void* dst, const void* src, uint32_t byte
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar)));
 }
-__device__ __forceinline__ bool p_test(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity));
-  return ok != 0;
-}
 
 // Copy tile t of stage S into the ring slot at `base`.
-__device__ __forceinline__ void issue_tile(const StepStage& S, const int (&sel)[N_USED], int t, uint8_t* base,
-                                           uint64_t* bar) {
+__device__ __forceinline__ void issue_tile(const StepStage& S, const int* sel, int t, uint8_t* base, uint64_t* bar) {
   const int type = S.type;
   const int nseg = tile_nseg(type), segrows = tile_segrows(type);
   const int nb = S.W.nb, U = 4 * nb;
   const uint32_t row_q = 48u * U, row_sc = 4u * U, row_d = 2u * nb;
-  const bool d_bulk = type != ST_XDOWN;
+  const bool d_bulk = type != ST_XDOWN;  // 7-block rows: 14-byte d rows are read by the consumers
   const uint32_t R = nseg * segrows;
   const uint32_t sc_off = R * row_q, d_off = sc_off + R * row_sc;
   p_expect_tx(bar, R * (row_q + row_sc + (d_bulk ? row_d : 0)));
@@ -238,226 +235,162 @@ __device__ __forceinline__ void issue_tile(const StepStage& S, const int (&sel)[
   }
 }
 
-// Move cursor c to its next tile; false when it must wait (expert ids not
-// published yet) or the stage list is exhausted.
-__device__ __forceinline__ bool cursor_next(const StepParams& P, const StepStage* stg, Cursor& c, unsigned target) {
-  const int nst = P.nstages;
-  while (c.s < nst) {
-    if (!c.ready) {
-      const int type = stg[c.s].type;
-      if (!is_ring(type)) {
-        c.s++;
-        continue;
-      }
-      if (type == ST_XSWIGLU || type == ST_XDOWN) {
-        const unsigned* b = &P.ctl->bar[stg[c.s].dep];
-        // relaxed poll (no L1 invalidation), one acquire once it is reached
-        if (ld_relaxed(b) < target || ld_acquire(b) < target) return false;
+// The producer warp's lane 0: all ring tiles of this CTA, in stage order.
+// Returns the number of tiles issued; on abort it stops early.
+__device__ int producer(const StepParams& P, const StepStage* stg, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                        unsigned target) {
+  StepCtl* ctl = P.ctl;
+  int k = 0;
+  for (int s = 0; s < P.nstages; s++) {
+    const StepStage& S = stg[s];
+    const int type = S.type;
+    if (!is_ring(type)) continue;
+    int sel[N_USED] = {0, 0, 0, 0};
+    if (type == ST_XSWIGLU || type == ST_XDOWN) {
+      // the expert ids of this layer come from its router stage
+      if (!counter_wait(&ctl->bar[S.dep], target, ctl, 2u)) return k;
 #pragma unroll
-        for (int i = 0; i < N_USED; i++) c.sel[i] = __ldcg(&P.ctl->sel[i]);
-      }
-      tile_range(stg[c.s].ntiles, c.t, c.t1);
-      c.ready = 1;
+      for (int i = 0; i < N_USED; i++) sel[i] = __ldcg(&ctl->sel[i]);
     }
-    if (c.t < c.t1) return true;
-    c.s++;
-    c.ready = 0;
-  }
-  return false;
-}
-
-// Issue every tile the ring and the dependencies allow; never blocks.
-__device__ __forceinline__ void prod_poll(const StepParams& P, Cursor& shared_c, uint8_t* ring, uint64_t* full,
-                                          uint64_t* empty, unsigned target) {
-  const StepStage* stg = stage_table(ring);
-  Cursor c = shared_c;  // registers for the duration of the poll
-  bool moved = false;
-  while (cursor_next(P, stg, c, target)) {
-    const int st = c.k % RING, round = c.k / RING;
-    if (round > 0 && !p_test(&empty[st], (round - 1) & 1)) break;  // slot still being read
-    issue_tile(stg[c.s], c.sel, c.t, ring + st * SLOT, &full[st]);
-    c.t++;
-    c.k++;
-    moved = true;
-  }
-  if (moved || c.s != shared_c.s || c.ready != shared_c.ready) shared_c = c;
-}
-
-// Before an aborting CTA returns, thread 0 waits (time-bounded, ignoring the
-// abort flag) for the copies it issued but nobody consumed: the shared memory
-// they write must stay allocated until they land.
-__device__ void drain(const Cursor& pr, int k, uint64_t* full) {
-  for (int j = k; j < pr.k; j++) mbar_wait(&full[j % RING], (j / RING) & 1, nullptr);
-}
-
-// Thread 0's waits keep the producer going.
-__device__ bool t0_wait_bar(const StepParams& P, Cursor& pr, uint8_t* ring, uint64_t* full, uint64_t* empty, int s,
-                            unsigned target) {
-  WaitBudget wb;
-  for (uint32_t i = 0;; i++) {
-    prod_poll(P, pr, ring, full, empty, target);
-    if (ld_relaxed(&P.ctl->bar[s]) >= target && ld_acquire(&P.ctl->bar[s]) >= target) return true;
-    if ((i & 63u) == 63u && ld_vol(&P.ctl->abort)) return false;
-    if ((i & 63u) == 63u && wb.spent()) {
-      raise_abort(P.ctl, 2u);
-      return false;
+    int t0, t1;
+    tile_range(S.ntiles, t0, t1);
+    for (int t = t0; t < t1; t++, k++) {
+      const int st = k % RING, round = k / RING;
+      if (round > 0 && !ring_wait(&empty[st], (round - 1) & 1, ctl)) return k;
+      issue_tile(S, sel, t, ring + st * SLOT, &full[st]);
     }
   }
-}
-
-// Warp 0 waits for a full slot as one converged warp: lane 0 keeps producing,
-// and no lane sleeps in a suspending try_wait while the copy it waits for may
-// still have to be issued by lane 0 of the same warp.
-__device__ bool w0_wait_full(const StepParams& P, Cursor& pr, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                             int kk, unsigned target) {
-  WaitBudget wb;
-  const bool lead = threadIdx.x == 0;
-  for (uint32_t i = 0;; i++) {
-    if (lead) prod_poll(P, pr, ring, full, empty, target);
-    __syncwarp();
-    if (__all_sync(0xffffffffu, mbar_test(&full[kk % RING], (kk / RING) & 1))) return true;
-    if ((i & 63u) == 63u) {
-      int stop = 0;
-      if (lead) {
-        if (ld_vol(&P.ctl->abort)) stop = 1;
-        else if (wb.spent()) {
-          raise_abort(P.ctl, 3u);
-          stop = 1;
-        }
-      }
-      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
-    }
-  }
+  return k;
 }
 
 // ------------------------------------------------------------- consumers
-// RMS factor of x over DIM (all warps).
-__device__ float cons_rms(const float* x, float eps, float* red) {
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < DIM; i += NCW * 32) {
-    const float v = ldcg(x + i);
-    ss = fmaf(v, v, ss);
-  }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  cons_sync();
-  float t = 0.f;
-  for (int i = 0; i < NCW; i++) t += red[i];
-  cons_sync();
-  return 1.0f / sqrtf(t / (float)DIM + eps);
-}
-
-// Per-CTA shared state of the consumers. Values that live across a stage's
-// tile loop are kept here rather than in registers: the tile loop already
-// holds the 64-float activation unit per lane, and 16 warps leave 128
-// registers per thread.
 struct ConsShared {
   float red[NCW];
-  float res[2][24];  // per-tile row results (double-buffered by tile parity)
-  float bv[16];      // LMHEAD running argmax of epilogue thread r
-  int bi[16];
+  float bv[NCW];     // LMHEAD argmax per consumer warp
+  int bi[NCW];
   int sel[N_USED];   // expert ids / weights of the current routed stage
   float selw[N_USED];
-  unsigned long long tw, tc, te, ts;  // trace sums (thread 0)
   int flag;
+  unsigned long long tw, tc, ts;  // trace sums of consumer warp 0 (thread 0 only)
+  float part[PART_TILES * 24];  // dot results [local tile][tile row] finished at stage end
 };
 
-// One weight-ring stage. Returns false on abort.
-__device__ bool ring_stage(const StepParams& P, const StepStage& S, int sidx, uint8_t* ring, uint64_t* full,
-                           uint64_t* empty, int& k, ConsShared& cs, float* xsm, Cursor& pr, unsigned target) {
+// Stage the activation vector(s) of a ring stage into shared memory (RMS
+// normalised when the stage has a norm) and load this lane's unit into xr.
+template <int TYPE>
+__device__ __forceinline__ void stage_x(const StepParams& P, const StepStage& S, ConsShared& cs, float* xsm, float* xr,
+                                        int u, int vec) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NVEC = TYPE == ST_XDOWN ? N_USED : 1;
+  constexpr int LEN = TYPE == ST_XDOWN ? EXPERT_FF : (TYPE == ST_DOWN28 ? N_FF : DIM);
+  constexpr int UV = LEN / 64;
+  constexpr int NF4 = NVEC * LEN / 4;
+  constexpr int PER = (NF4 + NCW * 32 - 1) / (NCW * 32);
+  // stages whose input is RMS-normalised (the others read a gated / SwiGLU /
+  // attention vector as it is)
+  constexpr bool NORM = TYPE == ST_QKV || TYPE == ST_CONV || TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU ||
+                        TYPE == ST_LMHEAD;
+  if (NORM) {
+    static_assert(!NORM || PER == 1, "normalised inputs are DIM long");
+    const int f = threadIdx.x;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (f < NF4) v = __ldcg((const float4*)S.xin + f);
+    float ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, v.w * v.w)));
+    ss = warp_sum(ss);
+    if (lane == 0) cs.red[warp] = ss;
+    cons_sync();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCW; i++) t += cs.red[i];
+    const float inv = 1.0f / sqrtf(t / (float)DIM + P.eps);
+    if (f < NF4) {
+      const float4 g = __ldg((const float4*)S.norm + f);
+      v = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+      *(float4*)&xsm[xs_index(4 * f, UV)] = v;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int f = threadIdx.x + i * NCW * 32;
+      if (f < NF4) {
+        const float4 v = __ldcg((const float4*)S.xin + f);
+        const int vv = (4 * f) / LEN, kk = 4 * f - vv * LEN;
+        *(float4*)&xsm[vv * LEN + xs_index(kk, UV)] = v;
+      }
+    }
+  }
+  cons_sync();
+  {
+    const float* src = xsm + vec * LEN;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const float4 q = *(const float4*)&src[(j * UV + u) * 4];
+      xr[4 * j + 0] = q.x;
+      xr[4 * j + 1] = q.y;
+      xr[4 * j + 2] = q.z;
+      xr[4 * j + 3] = q.w;
+    }
+  }
+  cons_sync();  // xsm may be overwritten by the next stage's staging
+}
+
+// One weight-ring stage on the consumer side. Returns false on abort (agreed
+// by all consumer threads). Warp w computes tile row(s):
+//   QKV / RESID / LMHEAD : 16-row tiles, row w (finished at once)
+//   CONV                 : 8 channels x (b, c, x) = 24 rows, rows w and w+16 (w < 8)
+//   SWIGLU / XSWIGLU     : 8 gate rows then 8 up rows, row w
+//   XDOWN                : 4 experts x 4 output rows, row w (expert w/4)
+//   DOWN28               : 4 rows x 7168 = 4 quarters of 28 units; quarter w%4 of row w/4
+// Not inlined: one kernel body holding all eight instantiations needs more
+// registers than a thread has with 17 warps per SM; as separate functions
+// each tile loop is allocated on its own.
+template <int TYPE>
+__device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S, int sidx, uint8_t* ring,
+                                        uint64_t* full, uint64_t* empty, int& k, ConsShared& cs, float* xsm) {
   StepCtl* ctl = P.ctl;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nseg = tile_nseg(S.type), segrows = tile_segrows(S.type);
-  const int nb = S.W.nb, U = 4 * nb;
-  const uint32_t row_q = 48u * U, row_sc = 4u * U, row_d = 2u * nb;
-  const uint32_t R = nseg * segrows;
-  const uint32_t sc_off = R * row_q, d_off = sc_off + R * row_sc;
-  if ((S.type == ST_XSWIGLU || S.type == ST_XDOWN) && threadIdx.x < N_USED) {
+  constexpr int NSEG = TYPE == ST_CONV ? 3 : (TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU) ? 2 : TYPE == ST_XDOWN ? 4 : 1;
+  constexpr int SEGROWS = (TYPE == ST_CONV || TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU) ? 8
+                          : (TYPE == ST_XDOWN || TYPE == ST_DOWN28)                 ? 4
+                                                                                    : 16;
+  constexpr int R = NSEG * SEGROWS;
+  constexpr int NB = TYPE == ST_XDOWN ? 7 : TYPE == ST_DOWN28 ? 28 : 8;
+  constexpr int U = 4 * NB;
+  constexpr uint32_t ROW_Q = 48u * U, ROW_SC = 4u * U, ROW_D = 2u * NB;
+  constexpr uint32_t SC_OFF = R * ROW_Q, D_OFF = SC_OFF + R * ROW_SC;
+  constexpr bool PARTIAL = TYPE == ST_CONV || TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU || TYPE == ST_XDOWN ||
+                           TYPE == ST_DOWN28;
+  if ((TYPE == ST_XSWIGLU || TYPE == ST_XDOWN) && threadIdx.x < N_USED) {
     cs.sel[threadIdx.x] = __ldcg(&ctl->sel[threadIdx.x]);
     cs.selw[threadIdx.x] = __ldcg(&ctl->selw[threadIdx.x]);
   }
-  if (S.type == ST_LMHEAD && threadIdx.x >= 32 && threadIdx.x < 48) {
-    cs.bv[threadIdx.x - 32] = -INFINITY;
-    cs.bi[threadIdx.x - 32] = 0x7fffffff;
-  }
-  // unit owned by this lane and the stage's activation registers
-  int u = lane < U ? lane : -1;
-  if (S.type == ST_DOWN28) u = lane < 28 ? (warp & 3) * 28 + lane : -1;
+  // this lane's unit and the warp's x vector. Rows of 28 units leave lanes
+  // 28-31 idle: they compute a duplicate unit whose dot is dropped (branch-free
+  // code keeps the tile loop within the register budget)
+  constexpr int UL = TYPE == ST_DOWN28 ? 28 : (U < 32 ? U : 32);
+  const bool live = lane < UL;
+  const int u = (TYPE == ST_DOWN28 ? (warp & 3) * 28 : 0) + (live ? lane : lane - UL);
+  const int vec = TYPE == ST_XDOWN ? warp >> 2 : 0;
   float xr[64];
-  {
-    // Stage the activations once per CTA (one L2 read of the vector instead of
-    // one per warp), RMS-normalising on the way when the stage has a norm.
-    const int nvec = S.type == ST_XDOWN ? N_USED : 1;
-    const int len = (S.type == ST_XDOWN) ? S.ff : (S.type == ST_DOWN28 ? N_FF : DIM);
-    const int Uv = len / 64;
-    const int nf4 = nvec * len / 4;
-    constexpr int PER = (XS_FLOATS / 4 + NCW * 32 - 1) / (NCW * 32);
-    float4 v[PER];
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; i++) {
-      const int f = threadIdx.x + i * NCW * 32;
-      if (f < nf4) {
-        v[i] = __ldcg((const float4*)S.xin + f);
-        ss = fmaf(v[i].x, v[i].x, fmaf(v[i].y, v[i].y, fmaf(v[i].z, v[i].z, fmaf(v[i].w, v[i].w, ss))));
-      }
-    }
-    float inv = 1.f;
-    if (S.norm) {
-      ss = warp_sum(ss);
-      if (lane == 0) cs.red[warp] = ss;
-      cons_sync();
-      float t = 0.f;
-      for (int i = 0; i < NCW; i++) t += cs.red[i];
-      inv = 1.0f / sqrtf(t / (float)DIM + P.eps);
-    }
-#pragma unroll
-    for (int i = 0; i < PER; i++) {
-      const int f = threadIdx.x + i * NCW * 32;
-      if (f < nf4) {
-        float4 o = v[i];
-        if (S.norm) {
-          const float4 g = __ldg((const float4*)S.norm + f);
-          o = make_float4(o.x * inv * g.x, o.y * inv * g.y, o.z * inv * g.z, o.w * inv * g.w);
-        }
-        const int vec = (4 * f) / len, kk = 4 * f - vec * len;
-        *(float4*)&xsm[vec * len + xs_index(kk, Uv)] = o;
-      }
-    }
-    cons_sync();
-    if (u >= 0) {
-      const float* src = xsm + (S.type == ST_XDOWN ? (warp >> 2) * len : 0);
-#pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const float4 q = *(const float4*)&src[(j * Uv + u) * 4];
-        xr[4 * j + 0] = q.x;
-        xr[4 * j + 1] = q.y;
-        xr[4 * j + 2] = q.z;
-        xr[4 * j + 3] = q.w;
-      }
-    }
-    cons_sync();  // xsm may be overwritten by the next stage's staging
-  }
-  if (P.trace && threadIdx.x == 0) P.trace[((size_t)sidx * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS + 1] = gtime();
+  stage_x<TYPE>(P, S, cs, xsm, xr, u, vec);
+  const bool tr = P.trace && threadIdx.x == 0;
+  if (tr) P.trace[((size_t)sidx * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS + 1] = gtime();
+  // tile rows of this warp (DOWN28: row w/4 of the tile in the smem row order)
+  const int nrow = (TYPE == ST_CONV && warp < 8) ? 2 : 1;
+  const int srow0 = TYPE == ST_DOWN28 ? (warp >> 2) : warp;
   int t0, t1;
   tile_range(S.ntiles, t0, t1);
-  const bool tr = P.trace && threadIdx.x == 0;
-  if (tr) cs.tw = cs.tc = cs.te = 0;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  bool ok = true;
+  if (tr) cs.tw = cs.tc = 0;
   for (int t = t0; t < t1; t++, k++) {
     const int st = k % RING;
-    float* res = cs.res[k & 1];
-    // residual values this tile adds to, fetched before the compute
-    // epilogue thread r = threadIdx.x - 32 (warp 1): warp 0 also produces and
-    // should go straight on to the next tile
-    const int r = (int)threadIdx.x - 32;
-    float rold = 0.f;
-    if (S.type == ST_RESID && r >= 0 && r < 16)
-      rold = __ldcg(S.resid + t * 16 + r);
-    else if ((S.type == ST_XDOWN || S.type == ST_DOWN28) && r >= 0 && r < 4)
-      rold = __ldcg(S.resid + t * 4 + r);
     if (tr) cs.ts = clock64();
-    const bool ok = warp == 0 ? w0_wait_full(P, pr, ring, full, empty, k, target)
-                              : ring_wait(&full[st], (k / RING) & 1, ctl);
+    if (!ring_wait(&full[st], (k / RING) & 1, ctl)) {
+      ok = false;
+      break;
+    }
     if (tr) {
       const unsigned long long now = clock64();
       cs.tw += now - cs.ts;
@@ -465,111 +398,114 @@ __device__ bool ring_stage(const StepParams& P, const StepStage& S, int sidx, ui
       if (t == t0) P.trace[((size_t)sidx * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS + 2] = gtime();
     }
     const uint8_t* base = ring + st * SLOT;
-    // this warp's stage rows: one per tile (two for the 24-row conv tile)
-    const int srow0 = S.type == ST_DOWN28 ? (warp >> 2) : warp;
-    const int nrow = (R > 16 && warp + 16 < (int)R) ? 2 : 1;
-    float acc[2] = {0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-      if (!ok || r >= nrow || u < 0) continue;
-      const int srow = srow0 + 16 * r;
-      const uint4* qp = (const uint4*)(base + srow * row_q) + u;
-      const uint4 A = qp[0], B = qp[U], Q = qp[2 * U];
-      const uint32_t scw = *(const uint32_t*)(base + sc_off + srow * row_sc + 4 * u);
-      float d;
-      if (S.type == ST_XDOWN) {
-        const size_t row = (size_t)cs.sel[srow >> 2] * DIM + t * 4 + (srow & 3);
-        d = __half2float(__ldg(S.W.d + row * nb + (u >> 2)));
-      } else {
-        d = __half2float(*(const __half*)(base + d_off + srow * row_d + 2 * (u >> 2)));
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < nrow; r++) {
+      const int sr = srow0 + 16 * r;
+      float a;
+      {
+        const uint4* qp = (const uint4*)(base + sr * ROW_Q) + u;
+        const uint4 A = qp[0], B = qp[U], Q = qp[2 * U];
+        const uint32_t scw = *(const uint32_t*)(base + SC_OFF + sr * ROW_SC + 4 * u);
+        float d;
+        if (TYPE == ST_XDOWN) {
+          const size_t row = (size_t)cs.sel[sr >> 2] * DIM + t * 4 + (sr & 3);
+          d = __half2float(__ldg(S.W.d + row * NB + (u >> 2)));
+        } else {
+          d = __half2float(*(const __half*)(base + D_OFF + sr * ROW_D + 2 * (u >> 2)));
+        }
+        a = q6_unit_dot(A, B, Q, scw, d, xr);
+        if (!live) a = 0.f;
       }
-      acc[r] = q6_unit_dot(A, B, Q, scw, d, xr);
+      if (r == 0) acc0 = a;
+      else acc1 = a;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
-    acc[0] = warp_sum(acc[0]);
-    if (R > 16) acc[1] = warp_sum(acc[1]);
+    acc0 = warp_sum(acc0);
+    if (TYPE == ST_CONV) acc1 = warp_sum(acc1);
     if (lane == 0) {
-      res[S.type == ST_DOWN28 ? warp : srow0] = acc[0];
-      if (nrow == 2) res[srow0 + 16] = acc[1];
-    }
-    // CTA-wide barrier that also agrees on an abort, so no thread is left
-    // waiting at a later barrier for threads that already returned
-    if (__syncthreads_or(!ok)) return false;
-    if (tr) {
-      const unsigned long long now = clock64();
-      cs.tc += now - cs.ts;
-      cs.ts = now;
-    }
-    // ------------------------------------------------------------ epilogues
-    if (r >= 0 && r < 16) switch (S.type) {
-      case ST_QKV: {
+      if (TYPE == ST_QKV) {
         int row0, ob;
         seg_src(S, cs.sel, t, 0, row0, ob);
-        if (r < 16) S.out[ob + row0 + r] = res[r];
-        break;
+        S.out[ob + row0 + warp] = acc0;
+      } else if (TYPE == ST_RESID) {
+        S.resid[t * 16 + warp] += acc0;  // this warp owns the row
+      } else if (TYPE == ST_LMHEAD) {
+        const int row = t * 16 + warp;
+        S.out[row] = acc0;
+        if (am_better(acc0, row, bv, bi)) {
+          bv = acc0;
+          bi = row;
+        }
+      } else if (TYPE == ST_DOWN28) {
+        cs.part[(t - t0) * 16 + (warp & 3) * 4 + (warp >> 2)] = acc0;  // [quarter][row]
+      } else if (PARTIAL) {
+        cs.part[(t - t0) * R + srow0] = acc0;
+        if (TYPE == ST_CONV && nrow == 2) cs.part[(t - t0) * R + srow0 + 16] = acc1;
       }
-      case ST_RESID:
-        if (r < 16) S.resid[t * 16 + r] = rold + res[r];
-        break;
-      case ST_LMHEAD:
-        if (r < 16) {
-          const int row = t * 16 + r;
-          const float v = res[r];
-          S.out[row] = v;
-          if (v > cs.bv[r] || (v == cs.bv[r] && row < cs.bi[r])) {
-            cs.bv[r] = v;
-            cs.bi[r] = row;
-          }
-        }
-        break;
-      case ST_CONV:
-        if (r < 8) {
-          // kernels/resident.rs:33-56; lfm.rs:464-520 for one token
-          const int ch = t * 8 + r;
-          const float bx = res[r] * res[16 + r];
-          const float s0 = S.state[2 * ch], s1 = S.state[2 * ch + 1];
-          float conv = 0.f;
-          conv += s0 * S.conv_w[3 * ch + 0];
-          conv += s1 * S.conv_w[3 * ch + 1];
-          conv += bx * S.conv_w[3 * ch + 2];
-          S.out[ch] = res[8 + r] * conv;
-          S.state[2 * ch] = s1;
-          S.state[2 * ch + 1] = bx;
-        }
-        break;
-      case ST_SWIGLU:
-        if (r < 8) S.out[t * 8 + r] = res[r] / (1.0f + expf(-res[r])) * res[8 + r];
-        break;
-      case ST_XSWIGLU:
-        if (r < 8) {
-          const int per = S.ff / 8, slot = t / per;
-          S.out[(size_t)slot * S.ff + (t - slot * per) * 8 + r] = res[r] / (1.0f + expf(-res[r])) * res[8 + r];
-        }
-        break;
-      case ST_XDOWN:
-        // rank-ordered combine of the 4 slots (kernels/resident.rs:101-117)
-        if (r < 4) {
-          float a = 0.f;
-#pragma unroll
-          for (int s2 = 0; s2 < N_USED; s2++) a += res[s2 * 4 + r] * cs.selw[s2];
-          S.resid[t * 4 + r] = rold + a;
-        }
-        break;
-      case ST_DOWN28:
-        if (r < 4) S.resid[t * 4 + r] = rold + (((res[4 * r] + res[4 * r + 1]) + res[4 * r + 2]) + res[4 * r + 3]);
-        break;
-      default:
-        break;
     }
-    if (tr) cs.te += clock64() - cs.ts;
+    if (tr) cs.tc += clock64() - cs.ts;
+  }
+  if (TYPE == ST_LMHEAD && lane == 0) {
+    cs.bv[warp] = bv;
+    cs.bi[warp] = bi;
+  }
+  // all consumers agree on an abort (and see each other's partials) before
+  // the stage is finished
+  if (cons_sync_or(!ok)) return false;
+  if (PARTIAL) {
+    const int nt = t1 - t0;
+    if (TYPE == ST_CONV) {
+      // kernels/resident.rs:33-56; lfm.rs:464-520 for one token
+      for (int i = threadIdx.x; i < nt * 8; i += NCW * 32) {
+        const int lt = i >> 3, r = i & 7, ch = (t0 + lt) * 8 + r;
+        const float* pp = cs.part + lt * R;
+        const float bx = pp[r] * pp[16 + r];
+        const float s0 = S.state[2 * ch], s1 = S.state[2 * ch + 1];
+        float conv = 0.f;
+        conv += s0 * S.conv_w[3 * ch + 0];
+        conv += s1 * S.conv_w[3 * ch + 1];
+        conv += bx * S.conv_w[3 * ch + 2];
+        S.out[ch] = pp[8 + r] * conv;
+        S.state[2 * ch] = s1;
+        S.state[2 * ch + 1] = bx;
+      }
+    } else if (TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU) {
+      for (int i = threadIdx.x; i < nt * 8; i += NCW * 32) {
+        const int lt = i >> 3, r = i & 7, t = t0 + lt;
+        const float v = silu_mul(cs.part[lt * R + r], cs.part[lt * R + 8 + r]);
+        if (TYPE == ST_SWIGLU) {
+          S.out[t * 8 + r] = v;
+        } else {
+          const int per = S.ff / 8, slot = t / per;
+          S.out[(size_t)slot * S.ff + (t - slot * per) * 8 + r] = v;
+        }
+      }
+    } else {
+      // XDOWN: rank-ordered expert combine (kernels/resident.rs:101-117);
+      // DOWN28: the four quarters of the 7168-wide row in order
+      for (int i = threadIdx.x; i < nt * 4; i += NCW * 32) {
+        const int lt = i >> 2, r = i & 3;
+        const float* pp = cs.part + lt * 16;
+        float a;
+        if (TYPE == ST_XDOWN) {
+          a = 0.f;
+#pragma unroll
+          for (int s2 = 0; s2 < N_USED; s2++) a += pp[s2 * 4 + r] * cs.selw[s2];
+        } else {
+          a = ((pp[r] + pp[4 + r]) + pp[8 + r]) + pp[12 + r];
+        }
+        S.resid[(t0 + lt) * 4 + r] += a;
+      }
+    }
   }
   if (tr) {
     unsigned long long* rec = P.trace + ((size_t)sidx * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS;
     rec[4] = cs.tw;
     rec[5] = (unsigned long long)(t1 - t0);
     rec[6] = cs.tc;
-    rec[7] = cs.te;
+    rec[7] = 0;
   }
   return true;
 }
@@ -716,12 +652,11 @@ __device__ void route_top4(const float* lg, const float* bias, StepCtl* ctl) {
   }
 }
 
-__global__ void __launch_bounds__(NT, 1) k_step(StepParams P) {
+__global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint64_t full[RING], empty[RING];
   __shared__ StageSmem stsm;
   __shared__ ConsShared cs;
-  __shared__ Cursor prod;
   __shared__ float lgs[N_EXPERT];
   StepCtl* ctl = P.ctl;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -735,40 +670,51 @@ __global__ void __launch_bounds__(NT, 1) k_step(StepParams P) {
     const int words = P.nstages * (int)(sizeof(StepStage) / 8);
     for (int i = threadIdx.x; i < words; i += NT) dst[i] = __ldg(src + i);
   }
-  __syncthreads();
   if (threadIdx.x == 0) {
     for (int s = 0; s < RING; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCW);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prod.s = 0, prod.t = 0, prod.t1 = 0, prod.k = 0, prod.ready = 0;
-    prod_poll(P, prod, ring, full, empty, target);  // fill the ring
   }
   __syncthreads();
+
+  if (warp == PRODUCER) {
+    if (lane == 0) {
+      const int issued = producer(P, stg, ring, full, empty, target);
+      // every issued copy must land before the CTA may exit (bounded waits,
+      // regardless of the abort flag)
+      for (int j = issued > RING ? issued - RING : 0; j < issued; j++)
+        mbar_wait(&full[j % RING], (j / RING) & 1, nullptr);
+    }
+    return;
+  }
 
   const int pos = P.io[1];
   int k = 0;
   for (int s = 0; s < P.nstages; s++) {
     const StepStage& S = stg[s];
     if (s > 0) {
-      if (threadIdx.x == 0) cs.flag = t0_wait_bar(P, prod, ring, full, empty, s - 1, target) ? 1 : 0;
+      if (threadIdx.x == 0) cs.flag = counter_wait(&ctl->bar[s - 1], target, ctl, 2u) ? 1 : 0;
       cons_sync();
-      if (!cs.flag) {
-        if (threadIdx.x == 0) drain(prod, k, full);
-        return;
-      }
-      cons_sync();
+      if (!cs.flag) return;
     }
     if (P.trace && threadIdx.x == 0) P.trace[((size_t)s * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS] = gtime();
+    bool ok = true;
     switch (S.type) {
       case ST_EMBED:
         if (blockIdx.x == 0 && warp == 0) {
-          const int tok = P.io[0];
+          int tok = P.io[0];
+          // a device-side id outside the table raises the status word and
+          // reads row 0 instead
+          if ((unsigned)tok >= (unsigned)P.embd.rows) {
+            if (lane == 0) atomicExch(&ctl->err, 4u);
+            tok = 0;
+          }
           const int U = 4 * P.embd.nb;
           if (lane < U) {
             // kernels/resident.rs:4-18: one 64-weight unit per lane, written
-            // out four values at a time (no 64-float temporary)
+            // out four values at a time
             const uint4* qp = P.embd.q + (size_t)tok * 3 * U + lane;
             const uint4 A = qp[0], B = qp[U], Q = qp[2 * U];
             const uint32_t scw = P.embd.sc[(size_t)tok * U + lane];
@@ -804,11 +750,21 @@ __global__ void __launch_bounds__(NT, 1) k_step(StepParams P) {
       case ST_ROUTER:
         if (blockIdx.x < N_EXPERT) {
           const int e = blockIdx.x;
-          const float inv = cons_rms(S.xin, P.eps, cs.red);
+          float ss = 0.f;
+          for (int i = threadIdx.x; i < DIM; i += NCW * 32) {
+            const float v = ldcg(S.xin + i);
+            ss = fmaf(v, v, ss);
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) cs.red[warp] = ss;
+          cons_sync();
+          float tss = 0.f;
+          for (int i = 0; i < NCW; i++) tss += cs.red[i];
+          const float inv = 1.0f / sqrtf(tss / (float)DIM + P.eps);
+          cons_sync();
           const float* w = S.rw + (size_t)e * DIM;
           float a = 0.f;
-          for (int i = threadIdx.x; i < DIM; i += NCW * 32)
-            a = fmaf(__ldg(w + i), ldcg(S.xin + i) * inv * S.norm[i], a);
+          for (int i = threadIdx.x; i < DIM; i += NCW * 32) a = fmaf(__ldg(w + i), ldcg(S.xin + i) * inv * S.norm[i], a);
           a = warp_sum(a);
           if (lane == 0) cs.red[warp] = a;
           cons_sync();
@@ -829,22 +785,27 @@ __global__ void __launch_bounds__(NT, 1) k_step(StepParams P) {
           }
         }
         break;
-      default:
-        if (!ring_stage(P, S, s, ring, full, empty, k, cs, stsm.xs, prod, target)) {
-          if (threadIdx.x == 0) drain(prod, k, full);
-          return;
-        }
+      case ST_QKV: ok = ring_stage<ST_QKV>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_RESID: ok = ring_stage<ST_RESID>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_CONV: ok = ring_stage<ST_CONV>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_SWIGLU: ok = ring_stage<ST_SWIGLU>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_DOWN28: ok = ring_stage<ST_DOWN28>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_XSWIGLU: ok = ring_stage<ST_XSWIGLU>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_XDOWN: ok = ring_stage<ST_XDOWN>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      case ST_LMHEAD: ok = ring_stage<ST_LMHEAD>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
+      default: break;
     }
-    // arrive at this stage's barrier: after the CTA barrier (which orders every
-    // thread's global writes before thread 0), thread 0 fences at gpu scope
-    // and publishes the CTA's arrival.
+    if (!ok) return;
+    // arrive at this stage's barrier: after the consumer barrier (which orders
+    // every consumer's global writes before thread 0), thread 0 fences at gpu
+    // scope and publishes the CTA's arrival.
     cons_sync();
     if (threadIdx.x == 0) {
       if (S.type == ST_LMHEAD) {
         float cv = cs.bv[0];
         int ci = cs.bi[0];
-        for (int w = 1; w < 16; w++)
-          if (cs.bv[w] > cv || (cs.bv[w] == cv && cs.bi[w] < ci)) {
+        for (int w = 1; w < NCW; w++)
+          if (am_better(cs.bv[w], cs.bi[w], cv, ci)) {
             cv = cs.bv[w];
             ci = cs.bi[w];
           }
@@ -861,7 +822,7 @@ __global__ void __launch_bounds__(NT, 1) k_step(StepParams P) {
         for (unsigned c = 0; c < G; c++) {
           const float2 q = __ldcg(&ctl->am_part[c]);
           const int qi = __float_as_int(q.y);
-          if (q.x > cv || (q.x == cv && qi < ci)) {
+          if (am_better(q.x, qi, cv, ci)) {
             cv = q.x;
             ci = qi;
           }

@@ -47,10 +47,13 @@ struct StepStage {
 
 constexpr int STEP_MAX_STAGES = 192;
 constexpr int STEP_MAX_CTAS = 160;
+// Most tiles one CTA may own in a stage whose rows are finished at stage end
+// (short conv, SwiGLU, expert and dense down projections).
+constexpr int STEP_PART_TILES = 16;
 // Trace record per (stage, CTA): %globaltimer ns stamps [0] stage start, [1]
 // activations staged, [2] first weight tile ready, [3] arrival at the stage
-// barrier; SM clock cycles [4] total wait for weight tiles, [6] total tile
-// compute (ready -> results agreed), [7] total epilogue; [5] tiles.
+// barrier; SM clock cycles of consumer warp 0: [4] total wait for weight
+// tiles, [6] total tile compute and epilogue; [5] tiles; [7] unused.
 constexpr int STEP_TRACE_FIELDS = 8;
 
 // Device-resident control block (zeroed once; barrier counters only grow).

@@ -1,5 +1,6 @@
-"""The persistent decode step (one cooperative kernel per token, LFM_STEP=1)
-against the CPU oracle and against the kernel chain.
+"""The persistent decode step (one cooperative kernel per token, the default;
+LFM_STEP=0 selects the kernel chain) against the CPU oracle and against the
+kernel chain.
 
 Same contract as the full-model tests (engine/src/main.rs:174-195 greedy loop,
 identical tokens, per-step logits max-abs <= 1e-2), plus: a long
@@ -46,13 +47,18 @@ def test_step_path_selected(step_engine):
     assert info["step_stages"] == 1 + 6 * 3 + 18 * 2 + 2 * 2 + 22 * 3 + 1
 
 
-def test_step_greedy_matches_oracle(step_engine, synth_model, oracle_mod):
+@pytest.fixture(scope="module")
+def oracle_greedy(synth_model, oracle_mod):
     p = np.random.default_rng(0).integers(0, 128000, PROMPT_LEN).astype(np.uint32)
     o = oracle_mod.OracleEngine(synth_model, kv_f16=True)
     o.set_ctx(PROMPT_LEN + N_GEN + 16)
     otoks, ologits = o.greedy(p, N_GEN, EOS)
     o.close()
-    e = step_engine
+    return p, otoks, ologits
+
+
+def _greedy_matches(e, oracle_greedy):
+    p, otoks, ologits = oracle_greedy
     e.set_ctx(PROMPT_LEN + N_GEN + 16)
     e.reset_session()
     logits = [e.forward(p, 0)]
@@ -67,6 +73,20 @@ def test_step_greedy_matches_oracle(step_engine, synth_model, oracle_mod):
     g = np.stack(logits)
     assert g.shape == ologits.shape
     assert np.abs(g - ologits).max() <= LOGIT_TOL
+
+
+def test_step_greedy_matches_oracle(step_engine, oracle_greedy):
+    _greedy_matches(step_engine, oracle_greedy)
+
+
+def test_chain_greedy_matches_oracle(synth_model, cuda_lib, oracle_greedy):
+    """The kernel chain (LFM_STEP=0) on the same contract."""
+    e = _engine(synth_model, False)
+    try:
+        _greedy_matches(e, oracle_greedy)
+        assert e.info()["decode_path"].startswith("kernel-chain")
+    finally:
+        e.close()
 
 
 def test_step_decode_loop_matches_chain(step_engine, synth_model):
