@@ -484,9 +484,9 @@ void EngineImpl::build_step() {
       StepStage& d = add(ST_DOWN28);
       d.W = L.down, d.xin = sw, d.resid = x, d.ntiles = L.down.rows / 4;
     } else {
-      const int dep = (int)st.size();
-      StepStage& r = add(ST_ROUTER);
-      r.rw = L.router, r.bias = L.bias, r.xin = x, r.norm = L.ffn_norm;
+      // the residual stage just added publishes this layer's router partials
+      const int dep = (int)st.size() - 1;
+      st[dep].rw = L.router, st[dep].bias = L.bias, st[dep].norm = L.ffn_norm;
       StepStage& g = add(ST_XSWIGLU);
       g.W = L.gate_x, g.W2 = L.up_x, g.xin = x, g.norm = L.ffn_norm, g.out = sw, g.ff = EXPERT_FF;
       g.ntiles = N_USED * EXPERT_FF / 8, g.dep = dep;

@@ -11,9 +11,10 @@
 // tiles of ALL stages in order and streams them through a 4-slot
 // shared-memory ring with bulk async copies (cp.async.bulk, no multicast)
 // completed on mbarriers. It waits only for free ring slots and, before
-// routed-expert tiles, for the router stage (the expert ids), so the weight
-// stream of later stages is in flight while earlier stages compute and the
-// grid barriers never drain the HBM pipeline.
+// routed-expert tiles, for the residual stage that publishes the router
+// partials; from those it computes the layer's top-4 experts itself (there is
+// no router stage). The weight stream of later stages is in flight while
+// earlier stages compute and the grid barriers never drain the HBM pipeline.
 //
 // Warps 0-15 consume. Each holds the stage's activation unit in registers (one
 // 64-weight unit per lane, q6k.cuh layout) and computes one dot row of every
@@ -76,11 +77,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ unsigned ld_vol(const unsigned* p) { return *(volatile const unsigned*)p; }
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 // Stage descriptors live in shared memory, after the weight ring.
@@ -127,12 +123,12 @@ __device__ bool ring_wait(uint64_t* b, uint32_t parity, StepCtl* ctl) {
   }
 }
 
-// Bounded wait for a grid barrier counter (relaxed polls, one acquire once
-// reached: an acquire at gpu scope invalidates L1).
+// Bounded wait for a grid barrier counter (acquire polls: the load that sees
+// the target already orders everything after it).
 __device__ bool counter_wait(const unsigned* c, unsigned target, StepCtl* ctl, unsigned code) {
   WaitBudget wb;
   for (uint32_t i = 0;; i++) {
-    if (ld_relaxed(c) >= target && ld_acquire(c) >= target) return true;
+    if (ld_acquire(c) >= target) return true;
     if ((i & 15u) == 15u) {
       if (ld_vol(&ctl->abort)) return false;
       if (wb.spent()) {
@@ -235,46 +231,121 @@ __device__ __forceinline__ void issue_tile(const StepStage& S, const int* sel, i
   }
 }
 
-// The producer warp's lane 0: all ring tiles of this CTA, in stage order.
-// Returns the number of tiles issued; on abort it stops early.
+// Shared state of the consumers (and the producer's routing hand-off).
+struct ConsShared {
+  uint64_t route_bar;  // consumers -> producer: the current MoE layer's routing is in psel/pselw
+  float red[NCW];
+  float bv[NCW];     // LMHEAD argmax per consumer warp
+  int bi[NCW];
+  int psel[N_USED];  // expert ids / weights of the current MoE layer (producer -> consumers)
+  float pselw[N_USED];
+  int flag;
+  unsigned long long tw, tc, ts;  // trace sums of consumer warp 0 (thread 0 only)
+  float part[PART_TILES * 24];  // dot results [local tile][tile row] finished at stage end
+};
+
+// Routing of one MoE layer from the per-CTA router partials that the
+// preceding residual stage published (see ring_stage<ST_RESID>): logit_e =
+// (1/rms(x)) * sum_c part[c][e], summed over CTAs in a fixed order so that
+// every CTA selects the same experts; then the sigmoid top-4 of
+// kernels/resident.rs:58-99 (prob + bias ranks, first index wins ties,
+// weights renormalised with the 6.103515625e-5 clamp). Run by the 16 consumer
+// warps at the start of the expert gate/up stage; `buf` is scratch shared
+// memory of at least G * 33 floats. The result goes to cs.psel / cs.pselw and
+// the producer is released through cs.route_bar.
+__device__ void route_layer(const StepParams& P, const float* bias, ConsShared& cs, float* buf) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const StepCtl* ctl = P.ctl;
+  const int G = gridDim.x;
+  constexpr int W = N_EXPERT + 1;
+  // one round of loads: the G x 33 partials into shared memory
+  const float* src = &ctl->rpart[0][0];
+  for (int f = threadIdx.x; f < G * W; f += NCW * 32) buf[f] = __ldcg(src + f);
+  cons_sync();
+  // column sums in a fixed order: lane l adds CTAs l, l+32, ... then a fixed
+  // butterfly across the warp; warp w handles columns w, w+16, w+32
+  for (int e = warp; e < W; e += NCW) {
+    float v = 0.f;
+    for (int c = lane; c < G; c += 32) v += buf[c * W + e];
+    v = warp_sum(v);
+    if (lane == 0) buf[G * W + e] = v;
+  }
+  cons_sync();
+  if (warp == 0) {
+    const float ss = buf[G * W + N_EXPERT];
+    const float inv = 1.0f / sqrtf(ss / (float)DIM + P.eps);
+    const float prob = 1.0f / (1.0f + expf(-(buf[G * W + lane] * inv)));
+    float score = prob + bias[lane];
+    float ps[N_USED];
+    int ids[N_USED];
+#pragma unroll
+    for (int r = 0; r < N_USED; r++) {
+      float best = score;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+      const unsigned mk = __ballot_sync(0xffffffffu, score == best);
+      const int id = mk ? __ffs(mk) - 1 : 0;
+      ps[r] = __shfl_sync(0xffffffffu, prob, id);
+      ids[r] = id;
+      if (lane == id) score = -INFINITY;
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < N_USED; r++) sum += ps[r];
+    sum = fmaxf(sum, 6.103515625e-5f);
+#pragma unroll
+    for (int r = 0; r < N_USED; r++)
+      if (lane == r) {
+        cs.psel[r] = ids[r];
+        cs.pselw[r] = ps[r] / sum;
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&cs.route_bar);  // release: psel/pselw are written
+  }
+  cons_sync();  // buf is reused by the activation staging
+}
+
+// The producer warp: all ring tiles of this CTA, in stage order (lane 0
+// issues, the warp computes each MoE layer's routing). Returns the number of
+// tiles issued; on abort it stops early.
 __device__ int producer(const StepParams& P, const StepStage* stg, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                        unsigned target) {
+                        unsigned target, ConsShared& cs) {
   StepCtl* ctl = P.ctl;
+  const int lane = threadIdx.x & 31;
   int k = 0;
+  int sel[N_USED] = {0, 0, 0, 0};
+  int routed = -1;  // residual stage whose routing `sel` holds
+  uint32_t rphase = 0;
   for (int s = 0; s < P.nstages; s++) {
     const StepStage& S = stg[s];
     const int type = S.type;
     if (!is_ring(type)) continue;
-    int sel[N_USED] = {0, 0, 0, 0};
-    if (type == ST_XSWIGLU || type == ST_XDOWN) {
-      // the expert ids of this layer come from its router stage
-      if (!counter_wait(&ctl->bar[S.dep], target, ctl, 2u)) return k;
+    if ((type == ST_XSWIGLU || type == ST_XDOWN) && S.dep != routed) {
+      // the consumers compute this layer's routing at the start of its gate/up
+      // stage and release cs.route_bar (one phase per MoE layer)
+      int ok = 1;
+      if (lane == 0) ok = ring_wait(&cs.route_bar, rphase, ctl) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return k;
 #pragma unroll
-      for (int i = 0; i < N_USED; i++) sel[i] = __ldcg(&ctl->sel[i]);
+      for (int i = 0; i < N_USED; i++) sel[i] = cs.psel[i];
+      rphase ^= 1u;
+      routed = S.dep;
     }
     int t0, t1;
     tile_range(S.ntiles, t0, t1);
     for (int t = t0; t < t1; t++, k++) {
       const int st = k % RING, round = k / RING;
-      if (round > 0 && !ring_wait(&empty[st], (round - 1) & 1, ctl)) return k;
-      issue_tile(S, sel, t, ring + st * SLOT, &full[st]);
+      int ok = 1;
+      if (lane == 0 && round > 0) ok = ring_wait(&empty[st], (round - 1) & 1, ctl) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return k;
+      if (lane == 0) issue_tile(S, sel, t, ring + st * SLOT, &full[st]);
+      __syncwarp();
     }
   }
   return k;
 }
 
 // ------------------------------------------------------------- consumers
-struct ConsShared {
-  float red[NCW];
-  float bv[NCW];     // LMHEAD argmax per consumer warp
-  int bi[NCW];
-  int sel[N_USED];   // expert ids / weights of the current routed stage
-  float selw[N_USED];
-  int flag;
-  unsigned long long tw, tc, ts;  // trace sums of consumer warp 0 (thread 0 only)
-  float part[PART_TILES * 24];  // dot results [local tile][tile row] finished at stage end
-};
-
 // Stage the activation vector(s) of a ring stage into shared memory (RMS
 // normalised when the stage has a norm) and load this lane's unit into xr.
 template <int TYPE>
@@ -293,8 +364,12 @@ __device__ __forceinline__ void stage_x(const StepParams& P, const StepStage& S,
   if (NORM) {
     static_assert(!NORM || PER == 1, "normalised inputs are DIM long");
     const int f = threadIdx.x;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (f < NF4) v = __ldcg((const float4*)S.xin + f);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), g = v;
+    if (f < NF4) {
+      // both loads in flight together: one L2 round trip, not two
+      v = __ldcg((const float4*)S.xin + f);
+      g = __ldg((const float4*)S.norm + f);
+    }
     float ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, v.w * v.w)));
     ss = warp_sum(ss);
     if (lane == 0) cs.red[warp] = ss;
@@ -304,7 +379,6 @@ __device__ __forceinline__ void stage_x(const StepParams& P, const StepStage& S,
     for (int i = 0; i < NCW; i++) t += cs.red[i];
     const float inv = 1.0f / sqrtf(t / (float)DIM + P.eps);
     if (f < NF4) {
-      const float4 g = __ldg((const float4*)S.norm + f);
       v = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
       *(float4*)&xsm[xs_index(4 * f, UV)] = v;
     }
@@ -360,10 +434,6 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   constexpr uint32_t SC_OFF = R * ROW_Q, D_OFF = SC_OFF + R * ROW_SC;
   constexpr bool PARTIAL = TYPE == ST_CONV || TYPE == ST_SWIGLU || TYPE == ST_XSWIGLU || TYPE == ST_XDOWN ||
                            TYPE == ST_DOWN28;
-  if ((TYPE == ST_XSWIGLU || TYPE == ST_XDOWN) && threadIdx.x < N_USED) {
-    cs.sel[threadIdx.x] = __ldcg(&ctl->sel[threadIdx.x]);
-    cs.selw[threadIdx.x] = __ldcg(&ctl->selw[threadIdx.x]);
-  }
   // this lane's unit and the warp's x vector. Rows of 28 units leave lanes
   // 28-31 idle: they compute a duplicate unit whose dot is dropped (branch-free
   // code keeps the tile loop within the register budget)
@@ -371,6 +441,7 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   const bool live = lane < UL;
   const int u = (TYPE == ST_DOWN28 ? (warp & 3) * 28 : 0) + (live ? lane : lane - UL);
   const int vec = TYPE == ST_XDOWN ? warp >> 2 : 0;
+  if (TYPE == ST_XSWIGLU) route_layer(P, stage_table(ring)[S.dep].bias, cs, xsm);
   float xr[64];
   stage_x<TYPE>(P, S, cs, xsm, xr, u, vec);
   const bool tr = P.trace && threadIdx.x == 0;
@@ -409,7 +480,7 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
         const uint32_t scw = *(const uint32_t*)(base + SC_OFF + sr * ROW_SC + 4 * u);
         float d;
         if (TYPE == ST_XDOWN) {
-          const size_t row = (size_t)cs.sel[sr >> 2] * DIM + t * 4 + (sr & 3);
+          const size_t row = (size_t)cs.psel[sr >> 2] * DIM + t * 4 + (sr & 3);
           d = __half2float(__ldg(S.W.d + row * NB + (u >> 2)));
         } else {
           d = __half2float(*(const __half*)(base + D_OFF + sr * ROW_D + 2 * (u >> 2)));
@@ -427,7 +498,7 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
     if (lane == 0) {
       if (TYPE == ST_QKV) {
         int row0, ob;
-        seg_src(S, cs.sel, t, 0, row0, ob);
+        seg_src(S, cs.psel, t, 0, row0, ob);
         S.out[ob + row0 + warp] = acc0;
       } else if (TYPE == ST_RESID) {
         S.resid[t * 16 + warp] += acc0;  // this warp owns the row
@@ -454,6 +525,27 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   // all consumers agree on an abort (and see each other's partials) before
   // the stage is finished
   if (cons_sync_or(!ok)) return false;
+  if (TYPE == ST_RESID && S.rw != nullptr) {
+    // Router partials of the MoE layer that follows (its rmsnorm input is the
+    // residual this stage just finished): for the rows this CTA owns,
+    // sum_r W_router[e][r] * g[r] * x[r] per expert e and sum_r x[r]^2. The
+    // 1/rms factor is applied when the partials are reduced (route_layer).
+    // S.norm / S.rw / S.bias hold the FFN norm and router of that layer.
+    float a = 0.f, ss = 0.f;
+    for (int r = t0 * 16 + warp; r < t1 * 16; r += NCW) {
+      const float xv = __ldcg(S.resid + r);
+      a = fmaf(__ldg(S.rw + (size_t)lane * DIM + r), xv * __ldg(S.norm + r), a);
+      ss = fmaf(xv, xv, ss);
+    }
+    xsm[warp * (N_EXPERT + 1) + lane] = a;
+    if (lane == 0) xsm[warp * (N_EXPERT + 1) + N_EXPERT] = ss;
+    cons_sync();
+    if (threadIdx.x <= N_EXPERT) {
+      float t = 0.f;
+      for (int w = 0; w < NCW; w++) t += xsm[w * (N_EXPERT + 1) + threadIdx.x];
+      ctl->rpart[blockIdx.x][threadIdx.x] = t;
+    }
+  }
   if (PARTIAL) {
     const int nt = t1 - t0;
     if (TYPE == ST_CONV) {
@@ -492,7 +584,7 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
         if (TYPE == ST_XDOWN) {
           a = 0.f;
 #pragma unroll
-          for (int s2 = 0; s2 < N_USED; s2++) a += pp[s2 * 4 + r] * cs.selw[s2];
+          for (int s2 = 0; s2 < N_USED; s2++) a += pp[s2 * 4 + r] * cs.pselw[s2];
         } else {
           a = ((pp[r] + pp[4 + r]) + pp[8 + r]) + pp[12 + r];
         }
@@ -624,40 +716,11 @@ __device__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm,
   if (gt == 0) P.ctl->attn_cnt[kh] = 0;
 }
 
-// sigmoid top-4 of the 32 router logits (kernels/resident.rs:58-99)
-__device__ void route_top4(const float* lg, const float* bias, StepCtl* ctl) {
-  const int lane = threadIdx.x & 31;
-  const float prob = 1.0f / (1.0f + expf(-lg[lane]));
-  float score = prob + bias[lane];
-  float ps[N_USED];
-  int ids[N_USED];
-#pragma unroll
-  for (int r = 0; r < N_USED; r++) {
-    float best = score;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
-    const unsigned mk = __ballot_sync(0xffffffffu, score == best);
-    const int id = mk ? __ffs(mk) - 1 : 0;
-    ps[r] = __shfl_sync(0xffffffffu, prob, id);
-    ids[r] = id;
-    if (lane == id) score = -INFINITY;
-  }
-  float sum = 0.f;
-#pragma unroll
-  for (int r = 0; r < N_USED; r++) sum += ps[r];
-  sum = fmaxf(sum, 6.103515625e-5f);
-  if (lane < N_USED) {
-    ctl->sel[lane] = ids[lane];
-    ctl->selw[lane] = ps[lane] / sum;
-  }
-}
-
 __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint64_t full[RING], empty[RING];
   __shared__ StageSmem stsm;
   __shared__ ConsShared cs;
-  __shared__ float lgs[N_EXPERT];
   StepCtl* ctl = P.ctl;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned G = gridDim.x;
@@ -675,18 +738,18 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCW);
     }
+    mbar_init(&cs.route_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
   if (warp == PRODUCER) {
-    if (lane == 0) {
-      const int issued = producer(P, stg, ring, full, empty, target);
-      // every issued copy must land before the CTA may exit (bounded waits,
-      // regardless of the abort flag)
+    const int issued = producer(P, stg, ring, full, empty, target, cs);
+    // every issued copy must land before the CTA may exit (bounded waits,
+    // regardless of the abort flag)
+    if (lane == 0)
       for (int j = issued > RING ? issued - RING : 0; j < issued; j++)
         mbar_wait(&full[j % RING], (j / RING) & 1, nullptr);
-    }
     return;
   }
 
@@ -747,44 +810,6 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
           for (int a = a0 + g; a < a1; a += 2) attn_task(P, S, stsm.attn[g], g, a / nact, a % nact, pos, nact);
         break;
       }
-      case ST_ROUTER:
-        if (blockIdx.x < N_EXPERT) {
-          const int e = blockIdx.x;
-          float ss = 0.f;
-          for (int i = threadIdx.x; i < DIM; i += NCW * 32) {
-            const float v = ldcg(S.xin + i);
-            ss = fmaf(v, v, ss);
-          }
-          ss = warp_sum(ss);
-          if (lane == 0) cs.red[warp] = ss;
-          cons_sync();
-          float tss = 0.f;
-          for (int i = 0; i < NCW; i++) tss += cs.red[i];
-          const float inv = 1.0f / sqrtf(tss / (float)DIM + P.eps);
-          cons_sync();
-          const float* w = S.rw + (size_t)e * DIM;
-          float a = 0.f;
-          for (int i = threadIdx.x; i < DIM; i += NCW * 32) a = fmaf(__ldg(w + i), ldcg(S.xin + i) * inv * S.norm[i], a);
-          a = warp_sum(a);
-          if (lane == 0) cs.red[warp] = a;
-          cons_sync();
-          if (threadIdx.x == 0) {
-            float t = 0.f;
-            for (int i = 0; i < NCW; i++) t += cs.red[i];
-            ctl->router_lg[e] = t;
-            __threadfence();
-            cs.flag = atomicAdd(&ctl->router_cnt, 1u) == (unsigned)(N_EXPERT - 1);
-          }
-          cons_sync();
-          if (cs.flag && warp == 0) {
-            __threadfence();
-            lgs[lane] = ldcg(&ctl->router_lg[lane]);
-            __syncwarp();
-            route_top4(lgs, S.bias, ctl);
-            if (lane == 0) ctl->router_cnt = 0;
-          }
-        }
-        break;
       case ST_QKV: ok = ring_stage<ST_QKV>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
       case ST_RESID: ok = ring_stage<ST_RESID>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
       case ST_CONV: ok = ring_stage<ST_CONV>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
@@ -811,9 +836,11 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
           }
         ctl->am_part[blockIdx.x] = make_float2(cv, __int_as_float(ci));
       }
-      __threadfence();
       if (P.trace) P.trace[((size_t)s * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS + 3] = gtime();
-      const unsigned prev = atomicAdd(&ctl->bar[s], 1u);
+      // release at gpu scope: every consumer's writes are ordered before this
+      // thread by the consumer barrier above
+      unsigned prev;
+      asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&ctl->bar[s]) : "memory");
       if (s == P.nstages - 1 && prev == target - 1) {
         // last CTA of the step: final argmax (kernels/persistent.rs:12-53)
         __threadfence();

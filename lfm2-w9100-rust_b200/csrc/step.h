@@ -17,7 +17,7 @@ enum StepStageType {
   ST_ATTN,        // head norm + rope + fp16 KV write + split attention + merge -> a
   ST_RESID,       // x += W in (o-proj, out_proj)
   ST_CONV,        // in_proj + short conv -> gated, rolls conv state
-  ST_ROUTER,      // router logits + sigmoid top-4 -> sel, selw
+  ST_ROUTER,      // (unused: routing is folded into the residual stage before each MoE FFN)
   ST_XSWIGLU,     // routed gate/up + SwiGLU -> sw[4][ff]
   ST_XDOWN,       // routed down + rank-ordered combine -> x += ...
   ST_SWIGLU,      // dense gate/up + SwiGLU -> sw
@@ -35,14 +35,14 @@ struct StepStage {
   float* resid;
   const float* conv_w;
   float* state;
-  const float* rw;   // router weights [32][2048]
-  const float* bias;
+  const float* rw;   // ST_RESID before an MoE FFN: that layer's router [32][2048] (norm = its ffn_norm)
+  const float* bias; // ... and expert bias
   const float* q_norm;
   const float* k_norm;
   __half* kc;
   __half* vc;
   int ff;            // expert ff / x stride
-  int dep;           // ST_XSWIGLU / ST_XDOWN: index of the router stage
+  int dep;           // ST_XSWIGLU / ST_XDOWN: index of the residual stage that publishes the routing
 };
 
 constexpr int STEP_MAX_STAGES = 192;
@@ -62,12 +62,11 @@ struct StepCtl {
   unsigned epoch;     // decode steps completed
   unsigned err;       // device status word: a bounded wait timed out
   unsigned abort;     // raised with err; every later wait returns at once
-  unsigned router_cnt;
   unsigned attn_cnt[KV_HEADS];
-  float router_lg[N_EXPERT];
-  int sel[N_USED];
-  float selw[N_USED];
   float2 am_part[STEP_MAX_CTAS];
+  // per-CTA router partials of the current MoE layer: 32 expert logits (before
+  // the 1/rms factor) and the sum of squares of the CTA's residual rows
+  float rpart[STEP_MAX_CTAS][N_EXPERT + 1];
 };
 
 struct StepParams {

@@ -44,7 +44,9 @@ def test_step_path_selected(step_engine):
     step_engine.forward(np.array([1, 2, 3], np.uint32), 0)
     info = step_engine.info()
     assert info["decode_path"] == "persistent-step", info
-    assert info["step_stages"] == 1 + 6 * 3 + 18 * 2 + 2 * 2 + 22 * 3 + 1
+    # embed; per layer mixer (QKV, ATTN, RESID or CONV, RESID) + FFN (SWIGLU,
+    # DOWN28 or XSWIGLU, XDOWN: routing is folded into the residual stage); lm_head
+    assert info["step_stages"] == 1 + 6 * 3 + 18 * 2 + 2 * 2 + 22 * 2 + 1
 
 
 @pytest.fixture(scope="module")
