@@ -1,7 +1,7 @@
 // TMA-staged Q6_K decode matvecs (sm_100a).
 //
 // One CTA per SM streams a contiguous range of row tiles from HBM into shared
-// memory with bulk asynchronous copies (cp.async.bulk, no multicast) issued by
+// memory with bulk asynchronous copies (cp.async.bulk, each CTA loading its own tiles) issued by
 // a dedicated producer warp and completed on mbarriers; eight consumer warps
 // compute from shared memory with the activations held in registers (one
 // 64-weight unit per lane, layout of q6k.cuh). Because weights do not depend

@@ -9,7 +9,7 @@
 //
 // Warp 8 of each CTA is a dedicated producer: it walks this CTA's weight
 // tiles of ALL stages in order and streams them through a 4-slot
-// shared-memory ring with bulk async copies (cp.async.bulk, no multicast)
+// shared-memory ring with bulk async copies (cp.async.bulk into this CTA only)
 // completed on mbarriers. It waits only for free ring slots and, before
 // routed-expert tiles, for the residual stage that publishes the router
 // partials; from those it computes the layer's top-4 experts itself (there is
