@@ -214,6 +214,15 @@ lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* s
  * wrong indices. */
 lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream);
 
+/* Tensor-core GEMM core of the prompt path (tcgen05 MMA, fp32 accumulation in
+ * tensor memory): c[i][j] = sum_k a[i][k] * b[j][k] for fp16 a [m][k] and
+ * b [n][k] (both row-major), fp32 c [m][n]. m % 128 == 0, n % 256 == 0,
+ * k % 64 == 0. Synchronous; LFM_ERR_DEVICE if a bounded wait timed out.
+ * Stands in for the reference's f32_matmul dispatch (kernels.rs:552-574)
+ * at the GEMM level; the Q6_K prompt GEMMs are built on it. */
+lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
+                           void* stream);
+
 /* Message of the last failing kernel-level call on this thread. */
 const char* lfm_ops_error(void);
 

@@ -11,6 +11,7 @@
 
 #include "../../include/lfm_cuda.h"
 #include "kernels.h"
+#include "tc_gemm.h"
 
 namespace {
 thread_local std::string t_err;
@@ -22,6 +23,9 @@ lfm_status cuda_status(cudaError_t e) {
 }
 
 bool shape_ok(uint32_t in_dim, uint32_t rows) { return in_dim >= 256 && in_dim % 256 == 0 && rows > 0; }
+
+// status word of lfm_tc_gemm_f16 (raised by a bounded wait that timed out)
+__device__ unsigned g_tc_err;
 }  // namespace
 
 extern "C" {
@@ -130,6 +134,31 @@ lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* s
   e = cudaGetLastError();
   cudaFreeAsync(scratch, s);
   return cuda_status(e);
+}
+
+lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
+                           void* stream) {
+  if (!a_dev || !b_dev || !c_dev || m == 0 || n == 0 || k == 0 || m % 128 || n % 256 || k % 64) {
+    t_err = "lfm_tc_gemm_f16: bad argument (m % 128, n % 256, k % 64 must be 0)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned* err = nullptr;
+  cudaError_t e = cudaGetSymbolAddress((void**)&err, g_tc_err);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = cudaMemsetAsync(err, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = lfm::tc_gemm_f16((const __half*)a_dev, (const __half*)b_dev, (int)m, (int)n, (int)k, c_dev, err, s);
+  if (e != cudaSuccess) return cuda_status(e);
+  unsigned h = 0;
+  e = cudaMemcpyAsync(&h, err, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (h) {
+    t_err = "lfm_tc_gemm_f16: a bounded wait in the kernel timed out";
+    return LFM_ERR_DEVICE;
+  }
+  return LFM_OK;
 }
 
 const char* lfm_ops_error(void) { return t_err.c_str(); }
