@@ -372,7 +372,7 @@ def main():
         prefill = {"prompt_len": PREFILL_LEN, "tok_s": round(ws * PREFILL_LEN / (pms / 1000), 1),
                    "ms": round(pms, 2), "tflops": round(fl / (pms / 1000) / 1e12, 2),
                    "frac_of_bf16_peak": round(fl / (pms / 1000) / 1e12 / peaks["bf16_tflops"], 4),
-                   "path": "FP32 CUDA-core Q6_K dequant GEMM"}
+                   "path": info.get("prefill_path", "")}
     micro = None
     if rank == 0 and not args.no_micro:
         micro = microbench(local)

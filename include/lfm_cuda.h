@@ -223,6 +223,26 @@ lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev,
 lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
                            void* stream);
 
+/* Tensor-core (tcgen05 / TMEM) Q6_K prompt GEMM, the prefill counterpart of
+ * lfm_q6k_matmul with the same contract: y[o + j*rows] = sum_k W[o,k]
+ * x[k + j*in_dim] for n columns (q6k_prompt, ops.rs:340-374). Weights enter
+ * the tensor cores as the integers sc*(q-32) with d applied per super-block,
+ * activations as an fp16 hi/lo pair; fp32 accumulation. rows % 128 == 0.
+ * Synchronous (scratch is allocated per call); LFM_ERR_DEVICE if a bounded
+ * wait timed out. */
+lfm_status lfm_q6k_prompt_gemm(const void* w_dev, uint32_t in_dim, uint32_t rows, const float* x_dev,
+                               uint32_t n, float* y_dev, void* stream);
+
+/* Grouped routed-expert form (q6k_grouped over expert_groups lists,
+ * resident_graph.rs:450-495): for token t < n and rank r < 4 with
+ * e = expert_ids[t*4 + r] and slot q = t*4 + r,
+ * y[q*rows + o] = sum_k W[e][o,k] x[(q / x_div)*in_dim + k]; x_div is 4 (one
+ * activation row per token, the gate/up input) or 1 (one per slot, the down
+ * input). n_expert == 32, rows % 128 == 0. Synchronous. */
+lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t n_expert,
+                                  const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_div,
+                                  uint32_t n, float* y_dev, void* stream);
+
 /* Message of the last failing kernel-level call on this thread. */
 const char* lfm_ops_error(void);
 

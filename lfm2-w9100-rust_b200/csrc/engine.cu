@@ -32,6 +32,7 @@
 #include "gguf.h"
 #include "kernels.h"
 #include "step.h"
+#include "tc_gemm.h"
 
 namespace lfm {
 
@@ -83,6 +84,9 @@ struct EngineImpl {
   bool use_graph = true;
   bool use_mvt = true;  // TMA-staged decode matvecs
   bool use_step = true;  // persistent decode step (LFM_STEP=0 selects the kernel chain)
+  bool use_tc = true;    // tensor-core Q6_K prompt GEMMs (LFM_PREFILL=fp32 selects the CUDA-core GEMMs)
+  int tc_min = 16;       // prompts of at least this many tokens use them (LFM_TC_MIN_TOKENS)
+  TcScratch tcs;
   std::string step_reason;  // why the persistent step is not in use
   StepCtl* ctl = nullptr;
   StepStage* d_stages = nullptr;
@@ -540,6 +544,14 @@ void EngineImpl::ensure_prefill(int n) {
   pselw = dalloc<float>(prefill_allocs, N * N_USED);
   pgroups = dalloc<int>(prefill_allocs, (size_t)N_EXPERT * (N + 1));
   pids = dalloc<uint32_t>(prefill_allocs, N);
+  // operand of the tensor-core prompt GEMMs: dense (K up to 7168) or grouped (K up to 2048)
+  tcs.rows = tc_scratch_rows(cap);
+  tcs.halves = std::max<size_t>(2 * ((N + 127) / 128 * 128) * N_FF, 2 * tcs.rows * DIM);
+  tcs.xg = dalloc<__half>(prefill_allocs, tcs.halves);
+  tcs.inv = dalloc<float>(prefill_allocs, tcs.rows);
+  tcs.tiles = dalloc<int>(prefill_allocs, 1 + 2 * (size_t)tc_max_tiles(cap));
+  tcs.slots = dalloc<int>(prefill_allocs, tcs.rows);
+  tcs.rowof = dalloc<int>(prefill_allocs, N * N_USED);
   ncap = cap;
 }
 
@@ -768,26 +780,42 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
   c.stream = s;
   c.pdl = false;
   c.sms = sms;
+  const bool tc = use_tc && n >= tc_min;
+  tcs.err = (unsigned*)(io + 4);
+  // x (n rows of K, stride K) -> activation operand of the tensor-core GEMMs
+  auto split = [&](const float* X, int K) {
+    CK(tc_split(X, K, K, n, tcs, s));
+    nl++;
+  };
+  // out[t * ldo + o] (+)= W x_t
+  auto mm = [&](const Q6Mat& W, const float* X, float* out, int ldo, bool resid) {
+    if (tc) CK(tc_gemm_q6(W, n, out, ldo, resid, tcs, s));
+    else gemm_q6_ld(W, X, n, out, ldo, resid, s);
+    nl++;
+  };
   for (uint32_t l = 0; l < hp.n_layers; l++) {
     const LayerW& L = layers[l];
     rmsnorm_n(px, L.attn_norm, eps, n, ph, s);
     nl++;
+    if (tc) split(ph, DIM);
     if (L.attn) {
       const int ld = DIM + 2 * KV_HEADS * HEAD_DIM;
-      gemm_q6_ld(L.q, ph, n, pqkv, ld, false, s);
-      gemm_q6_ld(L.k, ph, n, pqkv + DIM, ld, false, s);
-      gemm_q6_ld(L.v, ph, n, pqkv + DIM + KV_HEADS * HEAD_DIM, ld, false, s);
+      mm(L.q, ph, pqkv, ld, false);
+      mm(L.k, ph, pqkv + DIM, ld, false);
+      mm(L.v, ph, pqkv + DIM + KV_HEADS * HEAD_DIM, ld, false);
       __half* kcl = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
       __half* vcl = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
       qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kcl, vcl, s);
       attn_prefill(pqkv, kcl, vcl, start, n, ctx, pa, s);
-      gemm_q6(L.o, pa, n, px, true, s);
-      nl += 6;
+      if (tc) split(pa, DIM);
+      mm(L.o, pa, px, DIM, true);
+      nl += 2;
     } else {
-      gemm_q6(L.in_proj, ph, n, pbcx, false, s);
+      mm(L.in_proj, ph, pbcx, 3 * DIM, false);
       conv_prefill(pbcx, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, n, pgated, s);
-      gemm_q6(L.out_proj, pgated, n, px, true, s);
-      nl += 3;
+      if (tc) split(pgated, DIM);
+      mm(L.out_proj, pgated, px, DIM, true);
+      nl += 1;
     }
     const bool last = l == hp.n_layers - 1;
     if (last) {
@@ -799,19 +827,32 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
     rmsnorm_n(px, L.ffn_norm, eps, n, ph, s);
     nl++;
     if (L.dense) {
-      gemm_q6(L.gate, ph, n, pgate, false, s);
-      gemm_q6(L.up, ph, n, pup, false, s);
+      if (tc) split(ph, DIM);
+      mm(L.gate, ph, pgate, N_FF, false);
+      mm(L.up, ph, pup, N_FF, false);
       swiglu_n(pgate, pup, (size_t)n * N_FF, psw, s);
-      gemm_q6(L.down, psw, n, px, true, s);
-      nl += 4;
+      if (tc) split(psw, N_FF);
+      mm(L.down, psw, px, DIM, true);
+      nl += 1;
     } else {
       router_logits_n(L.router, ph, n, prlog, s);
       route_n(prlog, L.bias, N_EXPERT, n, psel, pselw, s);
       expert_groups(psel, n, pgroups, n, s);
-      gemm_q6_grouped(L.gate_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pgate, s);
-      gemm_q6_grouped(L.up_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pup, s);
-      swiglu_n(pgate, pup, (size_t)n * N_USED * EXPERT_FF, psw, s);
-      gemm_q6_grouped(L.down_x, DIM, psw, 1, pgroups, n, n, pdown, s);
+      if (tc) {
+        CK(tc_group(pgroups, n, n, tcs, s));
+        CK(tc_split_grouped(ph, DIM, N_USED, n, tcs, s));
+        CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, n, pgate, tcs, s));
+        CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, n, pup, tcs, s));
+        swiglu_n(pgate, pup, (size_t)n * N_USED * EXPERT_FF, psw, s);
+        CK(tc_split_grouped(psw, EXPERT_FF, 1, n, tcs, s));
+        CK(tc_gemm_q6_grouped(L.down_x, DIM, n, pdown, tcs, s));
+        nl += 3;
+      } else {
+        gemm_q6_grouped(L.gate_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pgate, s);
+        gemm_q6_grouped(L.up_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pup, s);
+        swiglu_n(pgate, pup, (size_t)n * N_USED * EXPERT_FF, psw, s);
+        gemm_q6_grouped(L.down_x, DIM, psw, 1, pgroups, n, n, pdown, s);
+      }
       combine_n(pdown, pselw, n, px, s);
       nl += 8;
       ctr.expert_grouped_launches += 3;
@@ -985,6 +1026,8 @@ lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out
   if (const char* v = getenv("LFM_GRAPH")) I.use_graph = std::string(v) != "0";
   if (const char* v = getenv("LFM_MVT")) I.use_mvt = std::string(v) != "0";
   if (const char* v = getenv("LFM_STEP")) I.use_step = std::string(v) != "0";
+  if (const char* v = getenv("LFM_PREFILL")) I.use_tc = std::string(v) != "fp32";
+  if (const char* v = getenv("LFM_TC_MIN_TOKENS")) I.tc_min = std::max(1, atoi(v));
   if (!I.use_step) I.step_reason = "persistent step disabled (LFM_STEP=0)";
   if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMallocHost(&I.h_io, 64) != cudaSuccess || cudaEventCreate(&I.ev0) != cudaSuccess ||
@@ -1144,7 +1187,9 @@ const char* lfm_engine_info(lfm_engine* e) {
            std::to_string(I.sms) + ", \"weight_bytes\": " + std::to_string(I.weight_bytes) + ", \"pdl\": " +
            (I.pdl ? "true" : "false") + ", \"graph\": " + (I.use_graph ? "true" : "false") +
            ", \"step_stages\": " + std::to_string(I.nstages) + ", \"launches_per_decode\": " +
-           std::to_string(I.launches_per_decode) + "}";
+           std::to_string(I.launches_per_decode) + ", \"prefill_path\": \"" +
+           (I.use_tc ? "tcgen05 Q6_K GEMM (n >= " + std::to_string(I.tc_min) + ")" : std::string("fp32 CUDA-core")) +
+           "\"}";
   return I.info.c_str();
 }
 

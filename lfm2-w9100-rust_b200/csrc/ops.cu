@@ -136,6 +136,91 @@ lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* s
   return cuda_status(e);
 }
 
+// Scratch of one synchronous prompt-GEMM call (stream-ordered allocations).
+struct CallScratch {
+  lfm::TcScratch sc;
+  void* mem = nullptr;
+  cudaStream_t s;
+  explicit CallScratch(cudaStream_t st) : s(st) {}
+  cudaError_t alloc(size_t rows, size_t K, size_t slots) {
+    sc.rows = rows;
+    sc.halves = 2 * rows * K;
+    const size_t tiles = 1 + 2 * (rows / 128 + 64);
+    const size_t bytes = sc.halves * 2 + rows * 4 + tiles * 4 + rows * 4 + slots * 4 + 256 * 5;
+    cudaError_t e = cudaMallocAsync(&mem, bytes, s);
+    if (e != cudaSuccess) return e;
+    char* p = (char*)mem;
+    auto take = [&](size_t b) {
+      char* r = p;
+      p += (b + 255) / 256 * 256;
+      return r;
+    };
+    sc.xg = (__half*)take(sc.halves * 2);
+    sc.inv = (float*)take(rows * 4);
+    sc.tiles = (int*)take(tiles * 4);
+    sc.slots = (int*)take(rows * 4);
+    sc.rowof = (int*)take(slots * 4);
+    return cudaGetSymbolAddress((void**)&sc.err, g_tc_err);
+  }
+  // zero the status word, run, read it back; frees the scratch
+  lfm_status finish(cudaError_t e, const char* who) {
+    if (e == cudaSuccess) {
+      unsigned h = 0;
+      e = cudaMemcpyAsync(&h, sc.err, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      if (e == cudaSuccess && h) {
+        if (mem) cudaFreeAsync(mem, s);
+        t_err = std::string(who) + ": a bounded wait in the kernel timed out";
+        return LFM_ERR_DEVICE;
+      }
+    }
+    if (mem) cudaFreeAsync(mem, s);
+    return cuda_status(e);
+  }
+};
+
+lfm_status lfm_q6k_prompt_gemm(const void* w_dev, uint32_t in_dim, uint32_t rows, const float* x_dev, uint32_t n,
+                               float* y_dev, void* stream) {
+  if (!w_dev || !x_dev || !y_dev || !shape_ok(in_dim, rows) || rows % 128 || n == 0 || n > (1u << 20)) {
+    t_err = "lfm_q6k_prompt_gemm: bad argument (rows % 128 == 0, 1 <= n <= 2^20)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
+  CallScratch cs(s);
+  cudaError_t e = cs.alloc((n + 127) / 128 * 128, in_dim, 1);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) e = lfm::tc_split(x_dev, (int)in_dim, (int)in_dim, (int)n, cs.sc, s);
+  if (e == cudaSuccess) e = lfm::tc_gemm_q6(W, (int)n, y_dev, (int)rows, false, cs.sc, s);
+  return cs.finish(e, "lfm_q6k_prompt_gemm");
+}
+
+lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t n_expert,
+                                  const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_div, uint32_t n,
+                                  float* y_dev, void* stream) {
+  if (!w_dev || !x_dev || !y_dev || !expert_ids_dev || !shape_ok(in_dim, rows) || rows % 128 ||
+      n_expert != (uint32_t)lfm::N_EXPERT || (x_div != 1 && x_div != (uint32_t)lfm::N_USED) || n == 0 ||
+      n > (1u << 16)) {
+    t_err = "lfm_q6k_prompt_grouped: bad argument (rows % 128 == 0, n_expert == 32, x_div 1 or 4, 1 <= n <= 65536)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)(rows * n_expert), (int)(in_dim / 256));
+  CallScratch cs(s);
+  int* groups = nullptr;
+  cudaError_t e = cs.alloc(lfm::tc_scratch_rows((int)n), in_dim, (size_t)n * lfm::N_USED);
+  if (e == cudaSuccess) e = cudaMallocAsync(&groups, sizeof(int) * (size_t)lfm::N_EXPERT * (n + 1), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) {
+    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s);
+    e = lfm::tc_group(groups, (int)n, (int)n, cs.sc, s);
+  }
+  if (e == cudaSuccess) e = lfm::tc_split_grouped(x_dev, (int)in_dim, (int)x_div, (int)n, cs.sc, s);
+  if (e == cudaSuccess) e = lfm::tc_gemm_q6_grouped(W, (int)rows, (int)n, y_dev, cs.sc, s);
+  if (groups) cudaFreeAsync(groups, s);
+  return cs.finish(e, "lfm_q6k_prompt_grouped");
+}
+
 lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
                            void* stream) {
   if (!a_dev || !b_dev || !c_dev || m == 0 || n == 0 || k == 0 || m % 128 || n % 256 || k % 64) {

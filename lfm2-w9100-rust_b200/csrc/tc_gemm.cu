@@ -165,6 +165,390 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ======================================================================
+// Q6_K prompt GEMM: out[t][o] (+)= sum_k W[o][k] x[t][k] for n tokens.
+//
+// Precision: the tensor cores multiply fp16 operands into fp32 sums, and an
+// fp16 copy of a Q6_K weight d*sc*(q-32) is not exact. The super-block scale
+// d is therefore kept out of the operand: A holds the integers sc*(q-32),
+// which fp16 holds exactly when |sc*(q-32)| <= 2048 or the product is even
+// (every weight with |sc| <= 64; above that, odd products round to the
+// nearest even integer, a relative error below 2^-11 on those weights only),
+// and each 256-wide super-block accumulates into its own TMEM accumulator
+// which the epilogue scales by d. The activations are split into an fp16 pair
+// hi + lo (about 22 significant bits) after a per-row power-of-two scaling
+// into fp16 range; hi and lo of 128 tokens form the 256 B-rows of one N=256
+// MMA, and the epilogue adds the two halves of the accumulator.
+//
+// Roles (14 warps):
+//   warp 0        TMA: raw Q6_K planes of the 128-row weight tile for each
+//                 super-block (3-D box over the quant plane, 2-D over the
+//                 scales; double-buffered) and 64-wide K chunks of the hi/lo
+//                 activations (3-stage ring)
+//   warp 1        TMEM allocation (512 columns: two 128 x 256 accumulators)
+//                 and the MMA issue: 4 x (M=128, N=256, K=16) per chunk
+//   warps 2-5     dequantisation: row r of the tile per thread, raw planes ->
+//                 fp16 sc*(q-32) in the swizzled K-major layout of the stage
+//   warps 6-13    epilogue: per super-block, tcgen05.ld of the accumulator,
+//                 y += d * (hi + lo); at the end the row's outputs are stored
+// Grouped (routed experts): the activations of each expert are gathered into
+// a contiguous, 128-padded run of hi/lo rows (tc_group, tc_split_grouped), a tile
+// table lists (expert, first row) per token tile, and the epilogue writes
+// each row to its selection slot.
+namespace {
+constexpr int QSTAGES = 3;
+constexpr int QA_BYTES = 128 * 128;          // A chunk: 128 rows x 64 fp16
+constexpr int QB_BYTES = 256 * 128;          // B chunk: 256 rows x 64 fp16
+constexpr int QSTAGE_BYTES = QA_BYTES + QB_BYTES;
+constexpr int RAWQ_BYTES = 128 * 3 * 64;     // quant pieces of 4 units x 128 rows
+constexpr int RAWS_BYTES = 128 * 16;         // scales of 4 units x 128 rows
+constexpr int RAW_BYTES = 26 * 1024;         // RAWQ + RAWS, 1 KB aligned
+constexpr int QTHREADS = 14 * 32;
+constexpr int QSMEM = QSTAGES * QSTAGE_BYTES + 2 * RAW_BYTES + 1024;
+constexpr uint32_t QTMEM_COLS = 512;
+
+struct TcQ6Params {
+  Q6Mat W;
+  int out_rows;        // rows per expert (grouped) or W.rows
+  int rpad;            // hi rows of the activation operand (lo rows follow)
+  const float* inv;    // [rpad] inverse activation scale per operand row
+  float* out;
+  int ldo;
+  int resid;
+  int ntok;            // dense: valid operand rows
+  const int* tiles;    // grouped: [0] = count, then (expert, first row) pairs
+  const int* slots;    // grouped: operand row -> output slot (-1: padding)
+  int grouped;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 4 codes (bytes of `code`) -> two half2 of sc*(code-32), exact.
+__device__ __forceinline__ void codes_to_h2(uint32_t code, __half2 sc2, uint32_t& lo, uint32_t& hi) {
+  const __half2 bias = __halves2half2(__float2half_rn(1056.f), __float2half_rn(1056.f));
+  // 0x64XX is the fp16 value 1024 + XX for XX < 256
+  uint32_t a = __byte_perm(code, 0x64646464u, 0x4140), b = __byte_perm(code, 0x64646464u, 0x4342);
+  __half2 ha = __hmul2(__hsub2(*(__half2*)&a, bias), sc2);
+  __half2 hb = __hmul2(__hsub2(*(__half2*)&b, bias), sc2);
+  lo = *(uint32_t*)&ha;
+  hi = *(uint32_t*)&hb;
+}
+
+__global__ void __launch_bounds__(QTHREADS, 1)
+    k_tc_q6(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapS,
+            const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* raw = smem + QSTAGES * QSTAGE_BYTES;
+  __shared__ uint64_t bfull[QSTAGES], afull[QSTAGES], empty[QSTAGES], raw_full[2], raw_empty[2], acc_full[2],
+      acc_empty[2], mma_done;
+  __shared__ uint32_t tmem_base;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.W.nb;
+  const int o0 = blockIdx.x * 128;
+  int brow0, wrow0;
+  if (p.grouped) {
+    if ((int)blockIdx.y >= p.tiles[0]) return;  // whole CTA leaves before any barrier or TMEM use
+    wrow0 = p.tiles[1 + 2 * blockIdx.y] * p.out_rows;
+    brow0 = p.tiles[2 + 2 * blockIdx.y];
+  } else {
+    wrow0 = 0;
+    brow0 = blockIdx.y * 128;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QSTAGES; s++) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&afull[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < 2; r++) {
+      mbar_init(&raw_full[r], 1);
+      mbar_init(&raw_empty[r], 4);
+      mbar_init(&acc_full[r], 1);
+      mbar_init(&acc_empty[r], 8);
+    }
+    mbar_init(&mma_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(QTMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ----------------------------------------------------------- producer
+      int issued_raw = 0, issued = 0;
+      bool ok = true;
+      for (int b = 0; b < nb && ok; b++) {
+        const int rb = b & 1;
+        if (b >= 2) ok = mbar_wait(&raw_empty[rb], ((b >> 1) - 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* rq = raw + rb * RAW_BYTES;
+        mbar_expect_tx(&raw_full[rb], RAWQ_BYTES + RAWS_BYTES);
+        tma_load_3d(rq, &mapQ, 64 * b, 0, wrow0 + o0, &raw_full[rb]);
+        tma_load_2d(rq + RAWQ_BYTES, &mapS, 16 * b, wrow0 + o0, &raw_full[rb]);
+        issued_raw = b + 1;
+        for (int c = 0; c < 4 && ok; c++) {
+          const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
+          if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, p.err);
+          if (!ok) break;
+          uint8_t* bs = smem + s * QSTAGE_BYTES + QA_BYTES;
+          mbar_expect_tx(&bfull[s], QB_BYTES);
+          tma_load_2d(bs, &mapX, 64 * j, brow0, &bfull[s]);
+          tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * j, p.rpad + brow0, &bfull[s]);
+          issued = j + 1;
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      for (int j = issued > QSTAGES ? issued - QSTAGES : 0; j < issued; j++)
+        mbar_wait(&bfull[j % QSTAGES], (j / QSTAGES) & 1, nullptr);
+      for (int b = issued_raw > 2 ? issued_raw - 2 : 0; b < issued_raw; b++)
+        mbar_wait(&raw_full[b & 1], (b >> 1) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // -------------------------------------------------------------- MMA
+      bool ok = true;
+      for (int b = 0; b < nb && ok; b++) {
+        const int a = b & 1;
+        if (b >= 2) ok = mbar_wait(&acc_empty[a], ((b >> 1) - 1) & 1, p.err);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(a * 256);
+        for (int c = 0; c < 4 && ok; c++) {
+          const int j = 4 * b + c, s = j % QSTAGES, ph = (j / QSTAGES) & 1;
+          ok = mbar_wait(&bfull[s], ph, p.err) && mbar_wait(&afull[s], ph, p.err);
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(smem + s * QSTAGE_BYTES), sb = sa + QA_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_f16(d, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), (c | kk) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[a]);
+      }
+      // tensor memory and the operand stages stay in use until every issued MMA has finished
+      mma_commit(&mma_done);
+      mbar_wait(&mma_done, 0, nullptr);
+    }
+  } else if (warp < 6) {
+    // -------------------------------------------------------- dequantise
+    const int r = threadIdx.x - 64;  // tile row
+    bool ok = true;
+    for (int b = 0; b < nb && ok; b++) {
+      const int rb = b & 1;
+      ok = mbar_wait(&raw_full[rb], (b >> 1) & 1, p.err);
+      if (!ok) break;
+      const uint8_t* rq = raw + rb * RAW_BYTES + r * 192;
+      const uint8_t* rs = raw + rb * RAW_BYTES + RAWQ_BYTES + r * 16;
+      for (int c = 0; c < 4 && ok; c++) {
+        const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
+        if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* arow = smem + s * QSTAGE_BYTES + r * 128;
+        const int h = c >> 1, m0 = 2 * (c & 1);
+#pragma unroll
+        for (int mm = 0; mm < 2; mm++) {
+          const int m = m0 + mm;
+#pragma unroll
+          for (int qq = 0; qq < 2; qq++) {
+            const int uu = 2 * h + qq;
+            const uint4 ql = *(const uint4*)(rq + (m & 1) * 64 + uu * 16);
+            const uint4 qh = *(const uint4*)(rq + 2 * 64 + uu * 16);
+            const float scf = (float)(int8_t)rs[uu * 4 + m];
+            const __half2 sc2 = __float2half2_rn(scf);
+            const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
+            uint32_t o[8];
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+              const uint32_t code = ((lw[w] >> (4 * (m >> 1))) & 0x0F0F0F0Fu) | (((hw[w] >> (2 * m)) & 0x03030303u) << 4);
+              codes_to_h2(code, sc2, o[2 * w], o[2 * w + 1]);
+            }
+            // 16 fp16 = two 16-byte pieces at chunk offset 32*mm + 16*qq elements
+            const int p0 = 4 * mm + 2 * qq;
+            *(uint4*)(arow + ((p0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *(uint4*)(arow + (((p0 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+        // generic-proxy writes -> visible to the tensor core's async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&raw_empty[rb]);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int g = (warp - 6) >> 2;   // token half: columns 64g..64g+63 (hi), 128+64g.. (lo)
+    const int quarter = warp & 3;    // TMEM lanes this warp may read
+    const int row = quarter * 32 + lane;
+    const size_t wrow = (size_t)wrow0 + o0 + row;
+    float y[64];
+#pragma unroll
+    for (int j = 0; j < 64; j++) y[j] = 0.f;
+    bool ok = true;
+    float dnext = __half2float(p.W.d[wrow * nb]);
+    for (int b = 0; b < nb; b++) {
+      const int a = b & 1;
+      const float d = dnext;
+      if (b + 1 < nb) dnext = __half2float(p.W.d[wrow * nb + b + 1]);
+      ok = ok && mbar_wait(&acc_full[a], (b >> 1) & 1, p.err);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * 256 + 64 * g);
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        uint32_t hi[16], lo[16];
+        tmem_ld16_nowait(base + 16 * h, hi);
+        tmem_ld16_nowait(base + 128 + 16 * h, lo);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; j++) y[16 * h + j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[16 * h + j]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (!ok) break;
+    }
+    if (ok) {
+      const int o = o0 + row;
+#pragma unroll
+      for (int j = 0; j < 64; j++) {
+        const int br = brow0 + 64 * g + j;
+        const float v = y[j] * __ldg(p.inv + br);
+        if (p.grouped) {
+          const int slot = __ldg(p.slots + br);
+          if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v;
+        } else if (br < p.ntok) {
+          float* dst = p.out + (size_t)br * p.ldo + o;
+          if (p.resid) *dst += v;
+          else *dst = v;
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(QTMEM_COLS));
+  }
+}
+
+// Activation operand. Block i handles source row i / x_div of X and writes
+// operand row r = rowof[i] (dense: r = i, x_div = 1) of the hi half and row
+// rpad + r of the lo half, after scaling the row by a power of two that
+// brings its largest magnitude into [2^13, 2^14); inv[r] undoes the scaling.
+// Operand rows that no block writes (tile padding) feed only output columns
+// that are never stored.
+__global__ void __launch_bounds__(256) k_tc_split(const float* X, int ldx, int K, int x_div, const int* rowof,
+                                                  int rpad, __half* xg, float* inv) {
+  const int i = blockIdx.x;
+  const int r = rowof ? rowof[i] : i;
+  if (r < 0 || r >= rpad) return;  // a slot whose expert id was out of range has no row
+  const float* xr = X + (size_t)(i / x_div) * ldx;
+  __shared__ float red[8];
+  float mx = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += 1024) {
+    const float4 v = *(const float4*)(xr + k);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
+  int ex = 0;
+  if (mx > 0.f && mx < 3.0e38f) {
+    frexpf(mx, &ex);               // mx < 2^ex
+    ex = min(max(14 - ex, -100), 100);
+  } else {
+    ex = 0;
+  }
+  const float sc = ldexpf(1.f, ex);
+  __half* hi = xg + (size_t)r * K;
+  __half* lo = xg + ((size_t)rpad + r) * K;
+  for (int k = threadIdx.x * 4; k < K; k += 1024) {
+    const float4 v = *(const float4*)(xr + k);
+    const float f[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
+    __half h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      h[j] = __float2half_rn(f[j]);
+      l[j] = __float2half_rn(f[j] - __half2float(h[j]));
+    }
+    __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+    __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+    *(uint2*)(hi + k) = make_uint2(*(uint32_t*)&h01, *(uint32_t*)&h23);
+    *(uint2*)(lo + k) = make_uint2(*(uint32_t*)&l01, *(uint32_t*)&l23);
+  }
+  if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
+}
+
+// Grouped layout from the expert lists (groups[e * (cap + 1)] = count, then
+// the selection slots): experts' rows start at 128-aligned bases; tiles =
+// {count, (expert, first row) ...}; slots[row] = selection slot or -1;
+// rowof[slot] = operand row. One block of 1024 threads.
+__global__ void k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots, int* rowof, int nslots,
+                                 int rpad) {
+  __shared__ int base[N_EXPERT], cnt[N_EXPERT];
+  const int t = threadIdx.x;
+  if (t < N_EXPERT) cnt[t] = groups[(size_t)t * (cap + 1)];
+  __syncthreads();
+  if (t == 0) {
+    int b = 0, nt = 0;
+    for (int e = 0; e < N_EXPERT; e++) {
+      base[e] = b;
+      const int tiles_e = (cnt[e] + 127) / 128;
+      for (int i = 0; i < tiles_e; i++) {
+        tiles[1 + 2 * nt] = e;
+        tiles[2 + 2 * nt] = b + 128 * i;
+        nt++;
+      }
+      b += 128 * tiles_e;
+    }
+    tiles[0] = nt;
+  }
+  for (int r = t; r < rpad; r += blockDim.x) slots[r] = -1;
+  for (int q = t; q < nslots; q += blockDim.x) rowof[q] = -1;
+  __syncthreads();
+  for (int e = 0; e < N_EXPERT; e++) {
+    const int* g = groups + (size_t)e * (cap + 1);
+    for (int i = t; i < cnt[e]; i += blockDim.x) {
+      const int slot = g[1 + i];
+      slots[base[e] + i] = slot;
+      rowof[slot] = base[e] + i;
+    }
+  }
+}
+
+}  // namespace
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda).
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -217,5 +601,120 @@ cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, f
   k_tc_f16<<<dim3(M / TM, N / TN), THREADS, smem, s>>>(ma, mb, C, M, N, K, err);
   return cudaGetLastError();
 }
+
+
+namespace {
+cudaError_t map_raw(CUtensorMap* mq, CUtensorMap* ms, const Q6Mat& W) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const int U = 4 * W.nb;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)U * 16, 3, (cuuint64_t)W.rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)U * 16, (cuuint64_t)U * 48};
+    const cuuint32_t box[3] = {64, 3, 128};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)W.q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)U * 4, (cuuint64_t)W.rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)U * 4};
+    const cuuint32_t box[2] = {16, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)W.sc, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
+}
+
+int dense_rpad(int n) { return (n + 127) / 128 * 128; }
+int grouped_rpad(int n) { return (int)tc_scratch_rows(n); }
+
+bool fits(const TcScratch& sc, int rpad, int K) {
+  return sc.xg && (size_t)rpad <= sc.rows && 2 * (size_t)rpad * (size_t)K <= sc.halves;
+}
+
+cudaError_t launch_q6(const Q6Mat& W, int rpad, int ntiles_y, const TcQ6Params& p, const TcScratch& sc,
+                      cudaStream_t s) {
+  CUtensorMap mq, ms, mx;
+  cudaError_t e = map_raw(&mq, &ms, W);
+  if (e != cudaSuccess) return e;
+  e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, 128);
+  if (e != cudaSuccess) return e;
+  static std::once_flag once;
+  std::call_once(once, [] { cudaFuncSetAttribute(k_tc_q6, cudaFuncAttributeMaxDynamicSharedMemorySize, QSMEM); });
+  k_tc_q6<<<dim3(p.out_rows / 128, ntiles_y), QTHREADS, QSMEM, s>>>(mq, ms, mx, p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+bool tc_q6_supported(const Q6Mat& W, int out_rows) {
+  return out_rows > 0 && out_rows % 128 == 0 && W.rows % out_rows == 0 && W.nb > 0 && encode_fn() != nullptr;
+}
+
+size_t tc_scratch_rows(int n) { return (size_t)n * N_USED + (size_t)N_EXPERT * 128 + 128; }
+
+cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s) {
+  const int rpad = dense_rpad(n);
+  if (n <= 0 || K % 64 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
+  k_tc_split<<<n, 256, 0, s>>>(X, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
+                       cudaStream_t s) {
+  const int rpad = dense_rpad(n);
+  if (n <= 0 || !fits(sc, rpad, W.nb * QK) || !tc_q6_supported(W, W.rows)) return cudaErrorInvalidValue;
+  TcQ6Params p = {};
+  p.W = W;
+  p.out_rows = W.rows;
+  p.rpad = rpad;
+  p.inv = sc.inv;
+  p.out = out;
+  p.ldo = ldo;
+  p.resid = resid ? 1 : 0;
+  p.ntok = n;
+  p.err = sc.err;
+  return launch_q6(W, rpad, rpad / 128, p, sc, s);
+}
+
+cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s) {
+  const int rpad = grouped_rpad(n);
+  if (n <= 0 || (size_t)rpad > sc.rows || !sc.tiles || !sc.slots || !sc.rowof) return cudaErrorInvalidValue;
+  k_tc_group_tiles<<<1, 1024, 0, s>>>(groups, cap, sc.tiles, sc.slots, sc.rowof, n * N_USED, rpad);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s) {
+  const int rpad = grouped_rpad(n);
+  if (n <= 0 || K % 64 || x_div <= 0 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
+  k_tc_split<<<n * N_USED, 256, 0, s>>>(X, K, K, x_div, sc.rowof, rpad, sc.xg, sc.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, const TcScratch& sc,
+                               cudaStream_t s) {
+  const int rpad = grouped_rpad(n);
+  if (n <= 0 || !fits(sc, rpad, W.nb * QK) || !tc_q6_supported(W, out_rows) || W.rows / out_rows > N_EXPERT)
+    return cudaErrorInvalidValue;
+  TcQ6Params p = {};
+  p.W = W;
+  p.out_rows = out_rows;
+  p.rpad = rpad;
+  p.inv = sc.inv;
+  p.out = out;
+  p.ldo = out_rows;
+  p.tiles = sc.tiles;
+  p.slots = sc.slots;
+  p.grouped = 1;
+  p.err = sc.err;
+  return launch_q6(W, rpad, tc_max_tiles(n), p, sc, s);
+}
+
+int tc_max_tiles(int n) { return (n * N_USED + 127) / 128 + N_EXPERT; }
 
 }  // namespace lfm

@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "kernels.h"
+
 namespace lfm {
 
 // K-major fp16 matrix [rows][K] as a TMA tensor map (64-wide K box, 128-byte swizzle).
@@ -12,5 +14,42 @@ cudaError_t tc_map_f16(CUtensorMap* map, const void* base, int rows, int K, int 
 // M % 128 == 0, N % 256 == 0, K % 64 == 0. *err is raised if a wait timed out.
 cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, float* C, unsigned* err,
                         cudaStream_t s);
+
+// Scratch of the Q6_K prompt GEMMs (engine-owned device memory): the hi/lo
+// activation operand, per-row inverse scales, and the grouped tile table,
+// row -> slot and slot -> row maps.
+struct TcScratch {
+  __half* xg = nullptr;  // hi rows [0, rpad) then lo rows [rpad, 2 rpad), K halves each
+  float* inv = nullptr;  // [rows]
+  int* tiles = nullptr;  // [1 + 2 * tc_max_tiles(n)]
+  int* slots = nullptr;  // [rows]
+  int* rowof = nullptr;  // [n * N_USED]
+  unsigned* err = nullptr;
+  size_t rows = 0;       // operand rows (tc_scratch_rows of the largest n)
+  size_t halves = 0;     // capacity of xg
+};
+// Operand rows needed for n tokens in the grouped case (n * 4 selection slots
+// plus 128-row padding per expert); the dense case needs n rounded up to 128.
+size_t tc_scratch_rows(int n);
+// Most token tiles a grouped GEMM of n tokens can have.
+int tc_max_tiles(int n);
+// The tensor-core path serves this matrix: 128-row output tiles.
+bool tc_q6_supported(const Q6Mat& W, int out_rows);
+
+// Dense: split rows [0, n) of X (row stride ldx, K columns) into the operand,
+// then out[t * ldo + o] (+)= sum_k W[o][k] X[t][k] for t < n, o < W.rows. One
+// split serves every GEMM on the same activations (q, k and v; gate and up).
+cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s);
+cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
+                       cudaStream_t s);
+
+// Routed experts: tc_group lays out the expert lists (groups[e * (cap + 1)] =
+// count, then selection slots t * 4 + rank), tc_split_grouped fills operand
+// row of slot q with X[q / x_div], and the GEMM writes, for expert e and each
+// of its slots, out[slot * out_rows + o] = sum_k W[e * out_rows + o][k] X[..][k].
+cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s);
+cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s);
+cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, const TcScratch& sc,
+                               cudaStream_t s);
 
 }  // namespace lfm
