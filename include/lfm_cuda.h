@@ -223,6 +223,13 @@ lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev,
 lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
                            void* stream);
 
+/* The same core with an MN-major second operand, the layout of the V cache
+ * (positions x 64 contiguous values): c[i][j] = sum_k a[i][k] * b[k][j] for
+ * fp16 a [m][k], b [k][64], fp32 c [m][64]; m % 128 == 0, k % 64 == 0.
+ * Synchronous. The P*V product of prompt attention (lfm.rs:425-437). */
+lfm_status lfm_tc_gemm_f16_bmn(const void* a_dev, const void* b_dev, uint32_t m, uint32_t k, float* c_dev,
+                               void* stream);
+
 /* Tensor-core (tcgen05 / TMEM) Q6_K prompt GEMM, the prefill counterpart of
  * lfm_q6k_matmul with the same contract: y[o + j*rows] = sum_k W[o,k]
  * x[k + j*in_dim] for n columns (q6k_prompt, ops.rs:340-374). Weights enter

@@ -815,7 +815,7 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       conv_prefill(pbcx, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, n, pgated, s);
       if (tc) split(pgated, DIM);
       mm(L.out_proj, pgated, px, DIM, true);
-      nl += 1;
+      nl += 2;
     }
     const bool last = l == hp.n_layers - 1;
     if (last) {

@@ -221,6 +221,21 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
   return cs.finish(e, "lfm_q6k_prompt_grouped");
 }
 
+lfm_status lfm_tc_gemm_f16_bmn(const void* a_dev, const void* b_dev, uint32_t m, uint32_t k, float* c_dev,
+                               void* stream) {
+  if (!a_dev || !b_dev || !c_dev || m == 0 || k == 0 || m % 128 || k % 64) {
+    t_err = "lfm_tc_gemm_f16_bmn: bad argument (m % 128, k % 64 must be 0)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  CallScratch cs(s);
+  cudaError_t e = cudaGetSymbolAddress((void**)&cs.sc.err, g_tc_err);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess)
+    e = lfm::tc_gemm_f16_bmn((const __half*)a_dev, (const __half*)b_dev, (int)m, (int)k, c_dev, cs.sc.err, s);
+  return cs.finish(e, "lfm_tc_gemm_f16_bmn");
+}
+
 lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uint32_t n, uint32_t k, float* c_dev,
                            void* stream) {
   if (!a_dev || !b_dev || !c_dev || m == 0 || n == 0 || k == 0 || m % 128 || n % 256 || k % 64) {

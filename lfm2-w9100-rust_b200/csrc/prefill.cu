@@ -156,24 +156,40 @@ __global__ void __launch_bounds__(256) k_rmsnorm_n(const float* x, const float* 
   for (int i = threadIdx.x; i < DIM; i += 256) out[(size_t)blockIdx.x * DIM + i] = xr[i] * inv * w[i];
 }
 
-// Short conv over n tokens, one thread per channel, serial in time like
-// kernels/resident.rs:33-56 (three taps over [state0, state1, b*x]).
-__global__ void k_conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated) {
+// Short conv over n tokens (kernels/resident.rs:33-56: three taps over
+// [state0, state1, b*x], the state rolling by one token per step). The taps
+// of token j are b*x of tokens j-2, j-1 (or the incoming state) and j, so
+// tokens are independent: thread (token, channel), same operation order as
+// the serial form. The new state is written by k_conv_state afterwards.
+__global__ void k_conv_prefill(const float* bcx, const float* conv_w, const float* state, int n, float* gated) {
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = blockIdx.y;
+  if (ch >= DIM || j >= n) return;
+  auto bx_of = [&](int t) {
+    const float* r = bcx + (size_t)t * 3 * DIM;
+    return r[ch] * r[2 * DIM + ch];
+  };
+  const float s0 = j >= 2 ? bx_of(j - 2) : (j == 1 ? state[2 * ch + 1] : state[2 * ch]);
+  const float s1 = j >= 1 ? bx_of(j - 1) : state[2 * ch + 1];
+  const float bx = bx_of(j);
+  float conv = 0.f;
+  conv += s0 * conv_w[3 * ch];
+  conv += s1 * conv_w[3 * ch + 1];
+  conv += bx * conv_w[3 * ch + 2];
+  gated[(size_t)j * DIM + ch] = bcx[(size_t)j * 3 * DIM + DIM + ch] * conv;
+}
+
+// Conv state after n tokens: (b*x of tokens n-2, n-1), or (old state1, b*x of
+// token 0) when n == 1.
+__global__ void k_conv_state(const float* bcx, float* state, int n) {
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= DIM) return;
-  float s0 = state[2 * ch], s1 = state[2 * ch + 1];
-  const float w0 = conv_w[3 * ch], w1 = conv_w[3 * ch + 1], w2 = conv_w[3 * ch + 2];
-  for (int j = 0; j < n; j++) {
-    const float* r = bcx + (size_t)j * 3 * DIM;
-    const float bx = r[ch] * r[2 * DIM + ch];
-    float conv = 0.f;
-    conv += s0 * w0;
-    conv += s1 * w1;
-    conv += bx * w2;
-    gated[(size_t)j * DIM + ch] = r[DIM + ch] * conv;
-    s0 = s1;
-    s1 = bx;
-  }
+  auto bx_of = [&](int t) {
+    const float* r = bcx + (size_t)t * 3 * DIM;
+    return r[ch] * r[2 * DIM + ch];
+  };
+  const float s0 = n >= 2 ? bx_of(n - 2) : state[2 * ch + 1];
+  const float s1 = bx_of(n - 1);
   state[2 * ch] = s0;
   state[2 * ch + 1] = s1;
 }
@@ -294,21 +310,33 @@ __global__ void k_router_logits_n(const float* Wr, const float* xn, int n, float
   if (lane == 0) logits[(size_t)j * N_EXPERT + e] = a;
 }
 
-// Stable per-expert slot lists (kernels/persistent.rs:58-76): warp e scans
-// slots (token*4 + rank) in order and appends those routed to e.
-__global__ void k_expert_groups(const int* sel, int n, int* groups, int cap) {
-  const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Stable per-expert slot lists (kernels/persistent.rs:58-76): block e scans
+// the slots (token*4 + rank) in order, 1024 at a time, and appends those
+// routed to e (ballot within warps, prefix over the block's warps).
+__global__ void __launch_bounds__(1024) k_expert_groups(const int* sel, int n, int* groups, int cap) {
+  __shared__ int wcount[32];
+  const int e = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   int* g = groups + (size_t)e * (cap + 1);
   int count = 0;
   const int total = n * N_USED;
-  for (int s0 = 0; s0 < total; s0 += 32) {
-    const int s = s0 + lane;
+  for (int s0 = 0; s0 < total; s0 += 1024) {
+    const int s = s0 + t;
     const bool hit = s < total && sel[s] == e;
     const unsigned m = __ballot_sync(0xffffffffu, hit);
-    if (hit) g[1 + count + __popc(m & ((1u << lane) - 1u))] = s;
-    count += __popc(m);
+    if (lane == 0) wcount[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, all = 0;
+#pragma unroll 8
+    for (int w = 0; w < 32; w++) {
+      const int c = wcount[w];
+      before += w < warp ? c : 0;
+      all += c;
+    }
+    if (hit) g[1 + count + before + __popc(m & ((1u << lane) - 1u))] = s;
+    count += all;
+    __syncthreads();
   }
-  if (lane == 0) g[0] = count;
+  if (t == 0) g[0] = count;
 }
 
 __global__ void k_swiglu_n(const float* gate, const float* up, size_t count, float* out) {
@@ -373,7 +401,8 @@ void rmsnorm_n(const float* x, const float* w, float eps, int n, float* out, cud
 }
 
 void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated, cudaStream_t s) {
-  k_conv_prefill<<<DIM / 128, 128, 0, s>>>(bcx, conv_w, state, n, gated);
+  k_conv_prefill<<<dim3(DIM / 256, n), 256, 0, s>>>(bcx, conv_w, state, n, gated);
+  k_conv_state<<<DIM / 256, 256, 0, s>>>(bcx, state, n);
 }
 
 void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int start, int n,
@@ -391,7 +420,7 @@ void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, 
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {
-  k_expert_groups<<<1, N_EXPERT * 32, 0, s>>>(sel, n, groups, cap);
+  k_expert_groups<<<N_EXPERT, 1024, 0, s>>>(sel, n, groups, cap);
 }
 
 void swiglu_n(const float* gate, const float* up, size_t count, float* out, cudaStream_t s) {

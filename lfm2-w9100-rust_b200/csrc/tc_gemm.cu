@@ -166,6 +166,117 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ======================================================================
+// MN-major B operand (the V tile of prompt attention, stored position-major:
+// B[k][n] with n contiguous): C[m][n] = sum_k A[m][k] B[k][n] for N = 64.
+// A 64-wide row of B is one 128-byte swizzle atom; a K chunk of 64 rows is
+// 8 groups of 8 rows at a 1024-byte stride (SBO), and the MMA's K steps of 16
+// rows advance the start address by 2048 bytes. The instruction descriptor
+// marks B as MN-major (bit 16).
+namespace {
+constexpr int BN_N = 64;
+constexpr uint32_t IDESC_BMN =
+    (1u << 4) | (1u << 16) | ((uint32_t)(BN_N >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+constexpr int BMN_A = TM * TK * 2, BMN_B = TK * BN_N * 2, BMN_STAGE = BMN_A + BMN_B;
+// the ring is followed by 32 KB that no operand uses
+constexpr int BMN_SMEM = STAGES * BMN_STAGE + 32768 + 1024;
+
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(8192 >> 4) << 16;   // leading byte offset: next 64-wide atom along N (none for N = 64)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next group of 8 K rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void mma_f16_desc(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_tc_f16_bmn(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, float* C,
+                 int M, int K, unsigned* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ uint64_t full[STAGES], empty[STAGES], acc_full;
+  __shared__ uint32_t tmem_base;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * TM;
+  const int nk = K / TK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(64));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  if (warp == 0 && lane == 0) {
+    int issued = 0;
+    for (int kc = 0; kc < nk; kc++) {
+      const int s = kc % STAGES, round = kc / STAGES;
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, err)) break;
+      uint8_t* a = smem + s * BMN_STAGE;
+      mbar_expect_tx(&full[s], BMN_STAGE);
+      tma_load_2d(a, &mapA, kc * TK, m0, &full[s]);
+      tma_load_2d(a + BMN_A, &mapB, 0, kc * TK, &full[s]);
+      issued = kc + 1;
+    }
+    for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; j++)
+      mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr);
+  } else if (warp == 1 && lane == 0) {
+    bool ok = true;
+    for (int kc = 0; kc < nk && ok; kc++) {
+      const int s = kc % STAGES;
+      ok = mbar_wait(&full[s], (kc / STAGES) & 1, err);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a = smem_u32(smem + s * BMN_STAGE), b = a + BMN_A;
+#pragma unroll
+      for (int kk = 0; kk < TK / 16; kk++)
+        mma_f16_desc(tmem, smem_desc_sw128(a + kk * 32), smem_desc_mn_sw128(b + kk * 2048), IDESC_BMN,
+                     (kc | kk) ? 1u : 0u);
+      mma_commit(&empty[s]);
+    }
+    mma_commit(&acc_full);
+    mbar_wait(&acc_full, 0, nullptr);
+  } else if (warp >= 2) {
+    const bool ok = mbar_wait(&acc_full, 0, err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    for (int c0 = 0; c0 < BN_N; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
+      if (ok && row < M)
+#pragma unroll
+        for (int j = 0; j < 32; j++) C[(size_t)row * BN_N + c0 + j] = __uint_as_float(r[j]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64));
+  }
+}
+}  // namespace
+
+// ======================================================================
 // Q6_K prompt GEMM: out[t][o] (+)= sum_k W[o][k] x[t][k] for n tokens.
 //
 // Precision: the tensor cores multiply fp16 operands into fp32 sums, and an
@@ -599,6 +710,20 @@ cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, f
     attr = true;
   }
   k_tc_f16<<<dim3(M / TM, N / TN), THREADS, smem, s>>>(ma, mb, C, M, N, K, err);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_gemm_f16_bmn(const __half* A, const __half* B, int M, int K, float* C, unsigned* err,
+                            cudaStream_t s) {
+  if (M % TM || K % TK || K <= 0) return cudaErrorInvalidValue;
+  CUtensorMap ma, mb;
+  cudaError_t e = tc_map_f16(&ma, A, M, K, TM);
+  if (e != cudaSuccess) return e;
+  e = tc_map_f16(&mb, B, K, BN_N, TK);  // B [K][64]: 64-wide rows, 64-row boxes
+  if (e != cudaSuccess) return e;
+  static std::once_flag once;
+  std::call_once(once, [] { cudaFuncSetAttribute(k_tc_f16_bmn, cudaFuncAttributeMaxDynamicSharedMemorySize, BMN_SMEM); });
+  k_tc_f16_bmn<<<M / TM, THREADS, BMN_SMEM, s>>>(ma, mb, C, M, K, err);
   return cudaGetLastError();
 }
 

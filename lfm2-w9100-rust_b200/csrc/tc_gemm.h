@@ -14,6 +14,11 @@ cudaError_t tc_map_f16(CUtensorMap* map, const void* base, int rows, int K, int 
 // M % 128 == 0, N % 256 == 0, K % 64 == 0. *err is raised if a wait timed out.
 cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, float* C, unsigned* err,
                         cudaStream_t s);
+// C[m][n] = sum_k A[m][k] B[k][n] for fp16 A [M][K] and B [K][64] (B
+// MN-major: rows of 64 contiguous values), fp32 C [M][64]. M % 128 == 0,
+// K % 64 == 0.
+cudaError_t tc_gemm_f16_bmn(const __half* A, const __half* B, int M, int K, float* C, unsigned* err,
+                            cudaStream_t s);
 
 // Scratch of the Q6_K prompt GEMMs (engine-owned device memory): the hi/lo
 // activation operand, per-row inverse scales, and the grouped tile table,

@@ -147,3 +147,22 @@ def test_prompt_gemm_rejects_bad_shapes(cuda_lib):
     y = torch.zeros(100, device="cuda")
     assert cuda_lib.lfm_q6k_prompt_gemm(_ptr(w), 2048, 100, _ptr(x), 1, _ptr(y), None) != 0
     assert cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), 2048, 128, 8, _ptr(x), _ptr(x), 4, 1, _ptr(y), None) != 0
+
+
+@pytest.mark.parametrize("m,k", [(128, 64), (256, 128), (128, 1024)])
+def test_tc_gemm_f16_mn_major_b(cuda_lib, m, k):
+    """MN-major second operand (rows of 64 contiguous values, like the V cache)."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(m * 7 + k)
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    b = rng.standard_normal((k, 64)).astype(np.float16)
+    ad, bd = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    c = torch.full((m, 64), float("nan"), device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_tc_gemm_f16_bmn(_ptr(ad), _ptr(bd), m, k, _ptr(c), None), "tc_gemm_f16_bmn")
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    got = c.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 1e-5, err
