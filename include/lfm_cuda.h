@@ -230,6 +230,16 @@ lfm_status lfm_tc_gemm_f16(const void* a_dev, const void* b_dev, uint32_t m, uin
 lfm_status lfm_tc_gemm_f16_bmn(const void* a_dev, const void* b_dev, uint32_t m, uint32_t k, float* c_dev,
                                void* stream);
 
+/* Causal GQA prompt attention on the tensor cores (the reference's prompt
+ * attention, lfm.rs:395-437 / kernels.rs:672-763): for token j < n at
+ * position start + j and query head h < 32 (KV head h / 4),
+ * out[j*out_stride + h*64 + d] = sum_t softmax_t(q.k_t / 8) v_t[d] over
+ * positions t <= start + j, with q at q_dev[j*q_stride + h*64 ..] (fp32) and
+ * the fp16 caches laid out [8][ctx][64]. Synchronous. */
+lfm_status lfm_attention_prefill(const float* q_dev, uint32_t q_stride, const void* k_cache, const void* v_cache,
+                                 uint32_t ctx, uint32_t start, uint32_t n, float* out_dev, uint32_t out_stride,
+                                 void* stream);
+
 /* Tensor-core (tcgen05 / TMEM) Q6_K prompt GEMM, the prefill counterpart of
  * lfm_q6k_matmul with the same contract: y[o + j*rows] = sum_k W[o,k]
  * x[k + j*in_dim] for n columns (q6k_prompt, ops.rs:340-374). Weights enter

@@ -806,7 +806,8 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       __half* kcl = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
       __half* vcl = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
       qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kcl, vcl, s);
-      attn_prefill(pqkv, kcl, vcl, start, n, ctx, pa, s);
+      if (tc) CK(attn_prefill_tc(pqkv, ld, kcl, vcl, (int)start, n, (int)ctx, pa, DIM, tcs.err, s));
+      else attn_prefill(pqkv, kcl, vcl, start, n, ctx, pa, s);
       if (tc) split(pa, DIM);
       mm(L.o, pa, px, DIM, true);
       nl += 2;
@@ -830,8 +831,11 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       if (tc) split(ph, DIM);
       mm(L.gate, ph, pgate, N_FF, false);
       mm(L.up, ph, pup, N_FF, false);
-      swiglu_n(pgate, pup, (size_t)n * N_FF, psw, s);
-      if (tc) split(psw, N_FF);
+      if (tc) {
+        CK(tc_split(pgate, N_FF, N_FF, n, tcs, s, pup));  // SwiGLU fused into the operand split
+      } else {
+        swiglu_n(pgate, pup, (size_t)n * N_FF, psw, s);
+      }
       mm(L.down, psw, px, DIM, true);
       nl += 1;
     } else {
@@ -843,10 +847,9 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
         CK(tc_split_grouped(ph, DIM, N_USED, n, tcs, s));
         CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, n, pgate, tcs, s));
         CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, n, pup, tcs, s));
-        swiglu_n(pgate, pup, (size_t)n * N_USED * EXPERT_FF, psw, s);
-        CK(tc_split_grouped(psw, EXPERT_FF, 1, n, tcs, s));
+        CK(tc_split_grouped(pgate, EXPERT_FF, 1, n, tcs, s, pup));  // SwiGLU fused into the operand split
         CK(tc_gemm_q6_grouped(L.down_x, DIM, n, pdown, tcs, s));
-        nl += 3;
+        nl += 2;  // group layout, first split (the fused split stands in for SwiGLU)
       } else {
         gemm_q6_grouped(L.gate_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pgate, s);
         gemm_q6_grouped(L.up_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pup, s);

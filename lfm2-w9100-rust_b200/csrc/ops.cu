@@ -221,6 +221,25 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
   return cs.finish(e, "lfm_q6k_prompt_grouped");
 }
 
+lfm_status lfm_attention_prefill(const float* q_dev, uint32_t q_stride, const void* k_cache, const void* v_cache,
+                                 uint32_t ctx, uint32_t start, uint32_t n, float* out_dev, uint32_t out_stride,
+                                 void* stream) {
+  if (!q_dev || !k_cache || !v_cache || !out_dev || n == 0 || ctx == 0 || (uint64_t)start + n > ctx ||
+      q_stride < (uint32_t)lfm::DIM || out_stride < (uint32_t)lfm::DIM || q_stride % 4 || out_stride % 4 ||
+      ctx > 65536) {
+    t_err = "lfm_attention_prefill: bad argument (start + n <= ctx <= 65536, strides >= 2048 and % 4 == 0)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  CallScratch cs(s);
+  cudaError_t e = cudaGetSymbolAddress((void**)&cs.sc.err, g_tc_err);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess)
+    e = lfm::attn_prefill_tc(q_dev, (int)q_stride, (const __half*)k_cache, (const __half*)v_cache, (int)start,
+                             (int)n, (int)ctx, out_dev, (int)out_stride, cs.sc.err, s);
+  return cs.finish(e, "lfm_attention_prefill");
+}
+
 lfm_status lfm_tc_gemm_f16_bmn(const void* a_dev, const void* b_dev, uint32_t m, uint32_t k, float* c_dev,
                                void* stream) {
   if (!a_dev || !b_dev || !c_dev || m == 0 || k == 0 || m % 128 || k % 64) {

@@ -27,11 +27,13 @@
 #include <mutex>
 
 #include "dev_common.cuh"
+#include "tc_common.cuh"
 #include "tc_gemm.h"
 
 namespace lfm {
 namespace {
 using namespace dev;
+using namespace tc;
 
 constexpr int TM = 128, TN = 256, TK = 64;  // tile and K chunk
 constexpr int STAGES = 4;
@@ -41,50 +43,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 6 * 32;
 constexpr uint32_t TMEM_COLS = 256;
 
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);          // start address
-  d |= (uint64_t)1 << 16;                           // leading byte offset (unused with swizzle): 16 B
-  d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: 8-row group = 1024 B
-  d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                           // layout: 128-byte swizzle
-  return d;
-}
-
 // kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both K-major.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(da), "l"(db), "r"(IDESC), "r"(accumulate));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+constexpr uint32_t IDESC = idesc_f16(TM, TN, false);
 
 __global__ void __launch_bounds__(THREADS, 1)
     k_tc_f16(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, float* C, int M,
@@ -138,7 +98,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
 #pragma unroll
       for (int kk = 0; kk < TK / 16; kk++)
-        mma_f16(tmem, smem_desc_sw128(a + kk * 32), smem_desc_sw128(b + kk * 32), (kc | kk) ? 1u : 0u);
+        mma_f16(tmem, smem_desc_sw128(a + kk * 32), smem_desc_sw128(b + kk * 32), IDESC, (kc | kk) ? 1u : 0u);
       mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
     }
     mma_commit(&acc_full);  // the accumulator is complete (or the loop gave up)
@@ -174,29 +134,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // marks B as MN-major (bit 16).
 namespace {
 constexpr int BN_N = 64;
-constexpr uint32_t IDESC_BMN =
-    (1u << 4) | (1u << 16) | ((uint32_t)(BN_N >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+constexpr uint32_t IDESC_BMN = idesc_f16(TM, BN_N, true);
 constexpr int BMN_A = TM * TK * 2, BMN_B = TK * BN_N * 2, BMN_STAGE = BMN_A + BMN_B;
 // the ring is followed by 32 KB that no operand uses
 constexpr int BMN_SMEM = STAGES * BMN_STAGE + 32768 + 1024;
-
-__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)(8192 >> 4) << 16;   // leading byte offset: next 64-wide atom along N (none for N = 64)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next group of 8 K rows
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-__device__ __forceinline__ void mma_f16_desc(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
     k_tc_f16_bmn(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, float* C,
@@ -248,7 +189,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a = smem_u32(smem + s * BMN_STAGE), b = a + BMN_A;
 #pragma unroll
       for (int kk = 0; kk < TK / 16; kk++)
-        mma_f16_desc(tmem, smem_desc_sw128(a + kk * 32), smem_desc_mn_sw128(b + kk * 2048), IDESC_BMN,
+        mma_f16(tmem, smem_desc_sw128(a + kk * 32), smem_desc_mn_sw128(b + kk * 2048), IDESC_BMN,
                      (kc | kk) ? 1u : 0u);
       mma_commit(&empty[s]);
     }
@@ -291,17 +232,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 // into fp16 range; hi and lo of 128 tokens form the 256 B-rows of one N=256
 // MMA, and the epilogue adds the two halves of the accumulator.
 //
-// Roles (14 warps):
+// Roles (10 warps):
 //   warp 0        TMA: raw Q6_K planes of the 128-row weight tile for each
 //                 super-block (3-D box over the quant plane, 2-D over the
 //                 scales; double-buffered) and 64-wide K chunks of the hi/lo
 //                 activations (3-stage ring)
 //   warp 1        TMEM allocation (512 columns: two 128 x 256 accumulators)
 //                 and the MMA issue: 4 x (M=128, N=256, K=16) per chunk
-//   warps 2-5     dequantisation: row r of the tile per thread, raw planes ->
-//                 fp16 sc*(q-32) in the swizzled K-major layout of the stage
-//   warps 6-13    epilogue: per super-block, tcgen05.ld of the accumulator,
-//                 y += d * (hi + lo); at the end the row's outputs are stored
+//   warps 2-9     workers, two per tile row: each reads its row's raw
+//                 pieces of a super-block once into registers and writes
+//                 half of every chunk's fp16 sc*(q-32) values into the
+//                 swizzled K-major stage; one chunk into the next super-
+//                 block it folds the finished accumulator into its 64
+//                 running sums, y += d * (hi + lo); at the end it stores them
 // Grouped (routed experts): the activations of each expert are gathered into
 // a contiguous, 128-padded run of hi/lo rows (tc_group, tc_split_grouped), a tile
 // table lists (expert, first row) per token tile, and the epilogue writes
@@ -314,7 +257,7 @@ constexpr int QSTAGE_BYTES = QA_BYTES + QB_BYTES;
 constexpr int RAWQ_BYTES = 128 * 3 * 64;     // quant pieces of 4 units x 128 rows
 constexpr int RAWS_BYTES = 128 * 16;         // scales of 4 units x 128 rows
 constexpr int RAW_BYTES = 26 * 1024;         // RAWQ + RAWS, 1 KB aligned
-constexpr int QTHREADS = 14 * 32;
+constexpr int QTHREADS = 10 * 32;
 constexpr int QSMEM = QSTAGES * QSTAGE_BYTES + 2 * RAW_BYTES + 1024;
 constexpr uint32_t QTMEM_COLS = 512;
 
@@ -332,23 +275,6 @@ struct TcQ6Params {
   int grouped;
   unsigned* err;
 };
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
 
 // 4 codes (bytes of `code`) -> two half2 of sc*(code-32), exact.
 __device__ __forceinline__ void codes_to_h2(uint32_t code, __half2 sc2, uint32_t& lo, uint32_t& hi) {
@@ -385,12 +311,12 @@ __global__ void __launch_bounds__(QTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < QSTAGES; s++) {
       mbar_init(&bfull[s], 1);
-      mbar_init(&afull[s], 4);
+      mbar_init(&afull[s], 8);
       mbar_init(&empty[s], 1);
     }
     for (int r = 0; r < 2; r++) {
       mbar_init(&raw_full[r], 1);
-      mbar_init(&raw_empty[r], 4);
+      mbar_init(&raw_empty[r], 8);
       mbar_init(&acc_full[r], 1);
       mbar_init(&acc_empty[r], 8);
     }
@@ -456,7 +382,7 @@ __global__ void __launch_bounds__(QTHREADS, 1)
           const uint32_t sa = smem_u32(smem + s * QSTAGE_BYTES), sb = sa + QA_BYTES;
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            mma_f16(d, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), (c | kk) ? 1u : 0u);
+            mma_f16(d, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), IDESC, (c | kk) ? 1u : 0u);
           mma_commit(&empty[s]);
         }
         mma_commit(&acc_full[a]);
@@ -465,85 +391,100 @@ __global__ void __launch_bounds__(QTHREADS, 1)
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0, nullptr);
     }
-  } else if (warp < 6) {
-    // -------------------------------------------------------- dequantise
-    const int r = threadIdx.x - 64;  // tile row
-    bool ok = true;
-    for (int b = 0; b < nb && ok; b++) {
-      const int rb = b & 1;
-      ok = mbar_wait(&raw_full[rb], (b >> 1) & 1, p.err);
-      if (!ok) break;
-      const uint8_t* rq = raw + rb * RAW_BYTES + r * 192;
-      const uint8_t* rs = raw + rb * RAW_BYTES + RAWQ_BYTES + r * 16;
-      for (int c = 0; c < 4 && ok; c++) {
-        const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
-        if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, p.err);
-        if (!ok) break;
-        uint8_t* arow = smem + s * QSTAGE_BYTES + r * 128;
-        const int h = c >> 1, m0 = 2 * (c & 1);
-#pragma unroll
-        for (int mm = 0; mm < 2; mm++) {
-          const int m = m0 + mm;
-#pragma unroll
-          for (int qq = 0; qq < 2; qq++) {
-            const int uu = 2 * h + qq;
-            const uint4 ql = *(const uint4*)(rq + (m & 1) * 64 + uu * 16);
-            const uint4 qh = *(const uint4*)(rq + 2 * 64 + uu * 16);
-            const float scf = (float)(int8_t)rs[uu * 4 + m];
-            const __half2 sc2 = __float2half2_rn(scf);
-            const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
-            uint32_t o[8];
-#pragma unroll
-            for (int w = 0; w < 4; w++) {
-              const uint32_t code = ((lw[w] >> (4 * (m >> 1))) & 0x0F0F0F0Fu) | (((hw[w] >> (2 * m)) & 0x03030303u) << 4);
-              codes_to_h2(code, sc2, o[2 * w], o[2 * w + 1]);
-            }
-            // 16 fp16 = two 16-byte pieces at chunk offset 32*mm + 16*qq elements
-            const int p0 = 4 * mm + 2 * qq;
-            *(uint4*)(arow + ((p0 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-            *(uint4*)(arow + (((p0 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-        }
-        // generic-proxy writes -> visible to the tensor core's async proxy
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[s]);
-      }
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&raw_empty[rb]);
-    }
   } else {
-    // ----------------------------------------------------------- epilogue
-    const int g = (warp - 6) >> 2;   // token half: columns 64g..64g+63 (hi), 128+64g.. (lo)
-    const int quarter = warp & 3;    // TMEM lanes this warp may read
+    // --------------------------------------------------------------- workers
+    // Thread (row, g): dequantises element pair m = 2 * (c & 1) + g of its
+    // tile row for every chunk c, and owns tokens 64g..64g+63 of that row in
+    // the epilogue (TMEM lanes of quarter warp % 4).
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const size_t wrow = (size_t)wrow0 + o0 + row;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(64 * g);
     float y[64];
 #pragma unroll
     for (int j = 0; j < 64; j++) y[j] = 0.f;
     bool ok = true;
-    float dnext = __half2float(p.W.d[wrow * nb]);
-    for (int b = 0; b < nb; b++) {
+    // y += d_b * (hi + lo) for super-block b's accumulator
+    auto epilogue = [&](int b, float d) {
       const int a = b & 1;
-      const float d = dnext;
-      if (b + 1 < nb) dnext = __half2float(p.W.d[wrow * nb + b + 1]);
       ok = ok && mbar_wait(&acc_full[a], (b >> 1) & 1, p.err);
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * 256 + 64 * g);
+      tc_fence_after();
+      const uint32_t base = lane_base + (uint32_t)(a * 256);
 #pragma unroll
       for (int h = 0; h < 4; h++) {
         uint32_t hi[16], lo[16];
         tmem_ld16_nowait(base + 16 * h, hi);
         tmem_ld16_nowait(base + 128 + 16 * h, lo);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; j++) y[16 * h + j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[16 * h + j]);
+        for (int j = 0; j < 16; j++)
+          y[16 * h + j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[16 * h + j]);
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
-      if (!ok) break;
+    };
+    // d of the super-block being folded, and of the one being dequantised
+    // (loaded a super-block ahead of its use)
+    float d_fold = 0.f, d_next = 0.f;
+    for (int b = 0; b < nb && ok; b++) {
+      const int rb = b & 1;
+      const uint8_t* rq = raw + rb * RAW_BYTES + row * 192;
+      d_fold = d_next;
+      d_next = __half2float(p.W.d[wrow * nb + b]);
+      uint4 ql[2], qh[2];
+      uint32_t scw[4];
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
+        const int h = c >> 1, m = 2 * (c & 1) + g;
+        if (c == 0) {
+          if (!(ok = mbar_wait(&raw_full[rb], (b >> 1) & 1, p.err))) break;
+          const uint4 sv = *(const uint4*)(raw + rb * RAW_BYTES + RAWQ_BYTES + row * 16);
+          scw[0] = sv.x, scw[1] = sv.y, scw[2] = sv.z, scw[3] = sv.w;
+        }
+        if ((c & 1) == 0) {
+          // this half's pieces: low nibbles (piece g) and high bits of units 2h, 2h+1
+#pragma unroll
+          for (int qq = 0; qq < 2; qq++) {
+            ql[qq] = *(const uint4*)(rq + g * 64 + (2 * h + qq) * 16);
+            qh[qq] = *(const uint4*)(rq + 128 + (2 * h + qq) * 16);
+          }
+          if (c == 2) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rb]);  // the raw block is in registers
+          }
+        }
+        if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1, p.err))) break;
+        uint8_t* arow = smem + s * QSTAGE_BYTES + row * 128;
+#pragma unroll
+        for (int qq = 0; qq < 2; qq++) {
+          const int uu = 2 * h + qq;
+          const float scf = (float)(int8_t)(uint8_t)(scw[uu] >> (8 * m));
+          const __half2 sc2 = __float2half2_rn(scf);
+          const uint32_t lw[4] = {ql[qq].x, ql[qq].y, ql[qq].z, ql[qq].w};
+          const uint32_t hw[4] = {qh[qq].x, qh[qq].y, qh[qq].z, qh[qq].w};
+          uint32_t o[8];
+#pragma unroll
+          for (int w = 0; w < 4; w++) {
+            const uint32_t code =
+                ((lw[w] >> (4 * (m >> 1))) & 0x0F0F0F0Fu) | (((hw[w] >> (2 * m)) & 0x03030303u) << 4);
+            codes_to_h2(code, sc2, o[2 * w], o[2 * w + 1]);
+          }
+          // 16 fp16 = two 16-byte pieces at chunk offset 32*g + 16*qq elements
+          const int p0 = 4 * g + 2 * qq;
+          *(uint4*)(arow + ((p0 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *(uint4*)(arow + (((p0 + 1) ^ (row & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+        // the previous super-block's accumulator is complete by now: fold it in
+        if (c == 1 && b >= 1) epilogue(b - 1, d_fold);
+      }
     }
+    if (ok) epilogue(nb - 1, d_next);
     if (ok) {
       const int o = o0 + row;
 #pragma unroll
@@ -573,18 +514,28 @@ __global__ void __launch_bounds__(QTHREADS, 1)
 // operand row r = rowof[i] (dense: r = i, x_div = 1) of the hi half and row
 // rpad + r of the lo half, after scaling the row by a power of two that
 // brings its largest magnitude into [2^13, 2^14); inv[r] undoes the scaling.
+// With `up`, the row is first the SwiGLU product silu(X) * up (the
+// reference's swiglu kernel, kernels.rs:543-550, same float operations).
 // Operand rows that no block writes (tile padding) feed only output columns
 // that are never stored.
-__global__ void __launch_bounds__(256) k_tc_split(const float* X, int ldx, int K, int x_div, const int* rowof,
-                                                  int rpad, __half* xg, float* inv) {
+__global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* up, int ldx, int K, int x_div,
+                                                  const int* rowof, int rpad, __half* xg, float* inv) {
+  extern __shared__ float4 srow[];  // the row (K floats)
   const int i = blockIdx.x;
   const int r = rowof ? rowof[i] : i;
   if (r < 0 || r >= rpad) return;  // a slot whose expert id was out of range has no row
-  const float* xr = X + (size_t)(i / x_div) * ldx;
+  const size_t src = (size_t)(i / x_div) * ldx;
+  const float4* xr = (const float4*)(X + src);
+  const float4* ur = up ? (const float4*)(up + src) : nullptr;
   __shared__ float red[8];
   float mx = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    const float4 v = *(const float4*)(xr + k);
+  for (int k = threadIdx.x; k < K / 4; k += 256) {
+    float4 v = xr[k];
+    if (ur) {
+      const float4 u = ur[k];
+      v = make_float4(silu_mul(v.x, u.x), silu_mul(v.y, u.y), silu_mul(v.z, u.z), silu_mul(v.w, u.w));
+    }
+    srow[k] = v;
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
 #pragma unroll
@@ -596,7 +547,7 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, int ldx, int K
   for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
   int ex = 0;
   if (mx > 0.f && mx < 3.0e38f) {
-    frexpf(mx, &ex);               // mx < 2^ex
+    frexpf(mx, &ex);  // mx < 2^ex
     ex = min(max(14 - ex, -100), 100);
   } else {
     ex = 0;
@@ -604,8 +555,8 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, int ldx, int K
   const float sc = ldexpf(1.f, ex);
   __half* hi = xg + (size_t)r * K;
   __half* lo = xg + ((size_t)rpad + r) * K;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    const float4 v = *(const float4*)(xr + k);
+  for (int k = threadIdx.x; k < K / 4; k += 256) {
+    const float4 v = srow[k];
     const float f[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
     __half h[4], l[4];
 #pragma unroll
@@ -613,10 +564,10 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, int ldx, int K
       h[j] = __float2half_rn(f[j]);
       l[j] = __float2half_rn(f[j] - __half2float(h[j]));
     }
-    __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
-    __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
-    *(uint2*)(hi + k) = make_uint2(*(uint32_t*)&h01, *(uint32_t*)&h23);
-    *(uint2*)(lo + k) = make_uint2(*(uint32_t*)&l01, *(uint32_t*)&l23);
+    const __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+    const __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+    *(uint2*)(hi + 4 * k) = make_uint2(*(const uint32_t*)&h01, *(const uint32_t*)&h23);
+    *(uint2*)(lo + 4 * k) = make_uint2(*(const uint32_t*)&l01, *(const uint32_t*)&l23);
   }
   if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
 }
@@ -783,10 +734,10 @@ bool tc_q6_supported(const Q6Mat& W, int out_rows) {
 
 size_t tc_scratch_rows(int n) { return (size_t)n * N_USED + (size_t)N_EXPERT * 128 + 128; }
 
-cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s) {
+cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s, const float* up) {
   const int rpad = dense_rpad(n);
-  if (n <= 0 || K % 64 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
-  k_tc_split<<<n, 256, 0, s>>>(X, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv);
+  if (n <= 0 || K % 64 || K > TC_SPLIT_KMAX || ldx % 4 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
+  k_tc_split<<<n, 256, K * 4, s>>>(X, up, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv);
   return cudaGetLastError();
 }
 
@@ -814,10 +765,11 @@ cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cud
   return cudaGetLastError();
 }
 
-cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s) {
+cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s,
+                             const float* up) {
   const int rpad = grouped_rpad(n);
-  if (n <= 0 || K % 64 || x_div <= 0 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
-  k_tc_split<<<n * N_USED, 256, 0, s>>>(X, K, K, x_div, sc.rowof, rpad, sc.xg, sc.inv);
+  if (n <= 0 || K % 64 || K > TC_SPLIT_KMAX || x_div <= 0 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
+  k_tc_split<<<n * N_USED, 256, K * 4, s>>>(X, up, K, K, x_div, sc.rowof, rpad, sc.xg, sc.inv);
   return cudaGetLastError();
 }
 

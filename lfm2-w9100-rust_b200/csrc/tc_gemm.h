@@ -20,6 +20,13 @@ cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, f
 cudaError_t tc_gemm_f16_bmn(const __half* A, const __half* B, int M, int K, float* C, unsigned* err,
                             cudaStream_t s);
 
+// Causal GQA prompt attention on the tensor cores for tokens [0, n) at
+// positions start.. (q of token j, head h at q + j*q_stride + h*64; K/V cache
+// [8][ctx][64] fp16 already holding positions 0..start+n-1); output at
+// out + j*out_stride + h*64.
+cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, const __half* vc, int start, int n,
+                            int ctx, float* out, int out_stride, unsigned* err, cudaStream_t s);
+
 // Scratch of the Q6_K prompt GEMMs (engine-owned device memory): the hi/lo
 // activation operand, per-row inverse scales, and the grouped tile table,
 // row -> slot and slot -> row maps.
@@ -44,7 +51,10 @@ bool tc_q6_supported(const Q6Mat& W, int out_rows);
 // Dense: split rows [0, n) of X (row stride ldx, K columns) into the operand,
 // then out[t * ldo + o] (+)= sum_k W[o][k] X[t][k] for t < n, o < W.rows. One
 // split serves every GEMM on the same activations (q, k and v; gate and up).
-cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s);
+// With `up` (same layout as X), the rows are the SwiGLU products silu(X) * up.
+constexpr int TC_SPLIT_KMAX = 12288;  // row length held in shared memory
+cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s,
+                     const float* up = nullptr);
 cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
                        cudaStream_t s);
 
@@ -53,7 +63,8 @@ cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, c
 // row of slot q with X[q / x_div], and the GEMM writes, for expert e and each
 // of its slots, out[slot * out_rows + o] = sum_k W[e * out_rows + o][k] X[..][k].
 cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s);
-cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s);
+cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s,
+                             const float* up = nullptr);
 cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, const TcScratch& sc,
                                cudaStream_t s);
 
