@@ -233,32 +233,35 @@ __global__ void __launch_bounds__(THREADS, 1)
 // MMA, and the epilogue adds the two halves of the accumulator.
 //
 // Roles (10 warps):
-//   warp 0        TMA: raw Q6_K planes of the 128-row weight tile for each
-//                 super-block (3-D box over the quant plane, 2-D over the
-//                 scales; double-buffered) and 64-wide K chunks of the hi/lo
-//                 activations (3-stage ring)
+//   warp 0        TMA: the raw Q6_K planes of the 128-row weight tile, half a
+//                 super-block at a time (3-D box over the quant plane; the
+//                 2-D scale box with the first half; two half buffers), and
+//                 64-wide K chunks of the hi/lo activations into a 5-deep
+//                 ring: the activation tiles come from L2/HBM with ~1.3 us
+//                 latency, and the ring keeps that many bytes in flight
 //   warp 1        TMEM allocation (512 columns: two 128 x 256 accumulators)
 //                 and the MMA issue: 4 x (M=128, N=256, K=16) per chunk
 //   warps 2-9     workers, two per tile row: each reads its row's raw
-//                 pieces of a super-block once into registers and writes
-//                 half of every chunk's fp16 sc*(q-32) values into the
-//                 swizzled K-major stage; one chunk into the next super-
-//                 block it folds the finished accumulator into its 64
+//                 pieces once per half super-block into registers and writes
+//                 half of every chunk's fp16 sc*(q-32) values into a 2-deep
+//                 ring of swizzled K-major A chunks; one chunk into the next
+//                 super-block it folds the finished accumulator into its 64
 //                 running sums, y += d * (hi + lo); at the end it stores them
 // Grouped (routed experts): the activations of each expert are gathered into
 // a contiguous, 128-padded run of hi/lo rows (tc_group, tc_split_grouped), a tile
 // table lists (expert, first row) per token tile, and the epilogue writes
 // each row to its selection slot.
 namespace {
-constexpr int QSTAGES = 3;
-constexpr int QA_BYTES = 128 * 128;          // A chunk: 128 rows x 64 fp16
-constexpr int QB_BYTES = 256 * 128;          // B chunk: 256 rows x 64 fp16
-constexpr int QSTAGE_BYTES = QA_BYTES + QB_BYTES;
-constexpr int RAWQ_BYTES = 128 * 3 * 64;     // quant pieces of 4 units x 128 rows
-constexpr int RAWS_BYTES = 128 * 16;         // scales of 4 units x 128 rows
-constexpr int RAW_BYTES = 26 * 1024;         // RAWQ + RAWS, 1 KB aligned
+constexpr int ASTAGES = 2;                    // dequantised A chunks (produced on chip)
+constexpr int BSTAGES = 5;                    // activation chunks (TMA from L2/HBM: the deep ring)
+constexpr int QA_BYTES = 128 * 128;           // A chunk: 128 rows x 64 fp16
+constexpr int QB_BYTES = 256 * 128;           // B chunk: 256 rows x 64 fp16
+constexpr int RAWH_Q = 128 * 3 * 32;          // half super-block: 3 pieces x 2 units x 128 rows
+constexpr int RAWH_S = 128 * 16;              // scales of the super-block (with the first half)
+constexpr int RAWH_BYTES = RAWH_Q + RAWH_S;   // 14 KB
+constexpr int OFF_B = ASTAGES * QA_BYTES, OFF_RAW = OFF_B + BSTAGES * QB_BYTES;
 constexpr int QTHREADS = 10 * 32;
-constexpr int QSMEM = QSTAGES * QSTAGE_BYTES + 2 * RAW_BYTES + 1024;
+constexpr int QSMEM = OFF_RAW + 2 * RAWH_BYTES + 1024;
 constexpr uint32_t QTMEM_COLS = 512;
 
 struct TcQ6Params {
@@ -292,9 +295,9 @@ __global__ void __launch_bounds__(QTHREADS, 1)
             const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* raw = smem + QSTAGES * QSTAGE_BYTES;
-  __shared__ uint64_t bfull[QSTAGES], afull[QSTAGES], empty[QSTAGES], raw_full[2], raw_empty[2], acc_full[2],
-      acc_empty[2], mma_done;
+  uint8_t* raw = smem + OFF_RAW;
+  __shared__ uint64_t bfull[BSTAGES], bempty[BSTAGES], afull[ASTAGES], aempty[ASTAGES], raw_full[2], raw_empty[2],
+      acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = p.W.nb;
@@ -309,10 +312,13 @@ __global__ void __launch_bounds__(QTHREADS, 1)
     brow0 = blockIdx.y * 128;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < QSTAGES; s++) {
+    for (int s = 0; s < BSTAGES; s++) {
       mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < ASTAGES; s++) {
       mbar_init(&afull[s], 8);
-      mbar_init(&empty[s], 1);
+      mbar_init(&aempty[s], 1);
     }
     for (int r = 0; r < 2; r++) {
       mbar_init(&raw_full[r], 1);
@@ -323,46 +329,44 @@ __global__ void __launch_bounds__(QTHREADS, 1)
     mbar_init(&mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(QTMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  if (warp == 1) tmem_alloc(&tmem_base, QTMEM_COLS);
+  tc_fence_before();
   __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  tc_fence_after();
   const uint32_t tmem = tmem_base;
+  const int nchunks = 4 * nb;
 
   if (warp == 0) {
     if (lane == 0) {
       // ----------------------------------------------------------- producer
-      int issued_raw = 0, issued = 0;
+      // Chunk j = 4b + c. Before the chunks of each half super-block
+      // (c = 0, 2), the raw pieces of that half go into raw buffer (half & 1).
+      int issued = 0, issued_raw = 0;
       bool ok = true;
-      for (int b = 0; b < nb && ok; b++) {
-        const int rb = b & 1;
-        if (b >= 2) ok = mbar_wait(&raw_empty[rb], ((b >> 1) - 1) & 1, p.err);
-        if (!ok) break;
-        uint8_t* rq = raw + rb * RAW_BYTES;
-        mbar_expect_tx(&raw_full[rb], RAWQ_BYTES + RAWS_BYTES);
-        tma_load_3d(rq, &mapQ, 64 * b, 0, wrow0 + o0, &raw_full[rb]);
-        tma_load_2d(rq + RAWQ_BYTES, &mapS, 16 * b, wrow0 + o0, &raw_full[rb]);
-        issued_raw = b + 1;
-        for (int c = 0; c < 4 && ok; c++) {
-          const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
-          if (round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, p.err);
-          if (!ok) break;
-          uint8_t* bs = smem + s * QSTAGE_BYTES + QA_BYTES;
-          mbar_expect_tx(&bfull[s], QB_BYTES);
-          tma_load_2d(bs, &mapX, 64 * j, brow0, &bfull[s]);
-          tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * j, p.rpad + brow0, &bfull[s]);
-          issued = j + 1;
+      for (int j = 0; j < nchunks && ok; j++) {
+        const int b = j >> 2, c = j & 3;
+        if ((c & 1) == 0) {
+          const int k = j >> 1, rb = k & 1;  // half super-block index
+          if (k >= 2 && !(ok = mbar_wait(&raw_empty[rb], ((k >> 1) - 1) & 1, p.err))) break;
+          uint8_t* rq = raw + rb * RAWH_BYTES;
+          mbar_expect_tx(&raw_full[rb], RAWH_Q + (c == 0 ? RAWH_S : 0));
+          tma_load_3d(rq, &mapQ, 64 * b + 32 * (c >> 1), 0, wrow0 + o0, &raw_full[rb]);
+          if (c == 0) tma_load_2d(rq + RAWH_Q, &mapS, 16 * b, wrow0 + o0, &raw_full[rb]);
+          issued_raw = k + 1;
         }
+        const int s = j % BSTAGES, round = j / BSTAGES;
+        if (round > 0 && !(ok = mbar_wait(&bempty[s], (round - 1) & 1, p.err))) break;
+        uint8_t* bs = smem + OFF_B + s * QB_BYTES;
+        mbar_expect_tx(&bfull[s], QB_BYTES);
+        tma_load_2d(bs, &mapX, 64 * j, brow0, &bfull[s]);
+        tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * j, p.rpad + brow0, &bfull[s]);
+        issued = j + 1;
       }
       // every issued copy must land before the CTA may exit
-      for (int j = issued > QSTAGES ? issued - QSTAGES : 0; j < issued; j++)
-        mbar_wait(&bfull[j % QSTAGES], (j / QSTAGES) & 1, nullptr);
-      for (int b = issued_raw > 2 ? issued_raw - 2 : 0; b < issued_raw; b++)
-        mbar_wait(&raw_full[b & 1], (b >> 1) & 1, nullptr);
+      for (int j = issued > BSTAGES ? issued - BSTAGES : 0; j < issued; j++)
+        mbar_wait(&bfull[j % BSTAGES], (j / BSTAGES) & 1, nullptr);
+      for (int k = issued_raw > 2 ? issued_raw - 2 : 0; k < issued_raw; k++)
+        mbar_wait(&raw_full[k & 1], (k >> 1) & 1, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -370,20 +374,20 @@ __global__ void __launch_bounds__(QTHREADS, 1)
       bool ok = true;
       for (int b = 0; b < nb && ok; b++) {
         const int a = b & 1;
-        if (b >= 2) ok = mbar_wait(&acc_empty[a], ((b >> 1) - 1) & 1, p.err);
-        if (!ok) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (b >= 2 && !(ok = mbar_wait(&acc_empty[a], ((b >> 1) - 1) & 1, p.err))) break;
+        tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * 256);
         for (int c = 0; c < 4 && ok; c++) {
-          const int j = 4 * b + c, s = j % QSTAGES, ph = (j / QSTAGES) & 1;
-          ok = mbar_wait(&bfull[s], ph, p.err) && mbar_wait(&afull[s], ph, p.err);
+          const int j = 4 * b + c, sb = j % BSTAGES, sa = j % ASTAGES;
+          ok = mbar_wait(&bfull[sb], (j / BSTAGES) & 1, p.err) && mbar_wait(&afull[sa], (j / ASTAGES) & 1, p.err);
           if (!ok) break;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = smem_u32(smem + s * QSTAGE_BYTES), sb = sa + QA_BYTES;
+          tc_fence_after();
+          const uint32_t ua = smem_u32(smem + sa * QA_BYTES), ub = smem_u32(smem + OFF_B + sb * QB_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            mma_f16(d, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), IDESC, (c | kk) ? 1u : 0u);
-          mma_commit(&empty[s]);
+            mma_f16(d, smem_desc_sw128(ua + kk * 32), smem_desc_sw128(ub + kk * 32), IDESC, (c | kk) ? 1u : 0u);
+          mma_commit(&bempty[sb]);
+          mma_commit(&aempty[sa]);
         }
         mma_commit(&acc_full[a]);
       }
@@ -429,35 +433,31 @@ __global__ void __launch_bounds__(QTHREADS, 1)
     // (loaded a super-block ahead of its use)
     float d_fold = 0.f, d_next = 0.f;
     for (int b = 0; b < nb && ok; b++) {
-      const int rb = b & 1;
-      const uint8_t* rq = raw + rb * RAW_BYTES + row * 192;
       d_fold = d_next;
       d_next = __half2float(p.W.d[wrow * nb + b]);
       uint4 ql[2], qh[2];
       uint32_t scw[4];
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        const int j = 4 * b + c, s = j % QSTAGES, round = j / QSTAGES;
+        const int j = 4 * b + c, s = j % ASTAGES, round = j / ASTAGES;
         const int h = c >> 1, m = 2 * (c & 1) + g;
-        if (c == 0) {
-          if (!(ok = mbar_wait(&raw_full[rb], (b >> 1) & 1, p.err))) break;
-          const uint4 sv = *(const uint4*)(raw + rb * RAW_BYTES + RAWQ_BYTES + row * 16);
-          scw[0] = sv.x, scw[1] = sv.y, scw[2] = sv.z, scw[3] = sv.w;
-        }
         if ((c & 1) == 0) {
-          // this half's pieces: low nibbles (piece g) and high bits of units 2h, 2h+1
+          // this half's pieces (low nibbles: piece g; high bits: piece 2) of units 2h, 2h+1
+          const int k = 2 * b + h, rb = k & 1;
+          if (!(ok = mbar_wait(&raw_full[rb], (k >> 1) & 1, p.err))) break;
+          const uint8_t* rq = raw + rb * RAWH_BYTES + row * 96;
 #pragma unroll
           for (int qq = 0; qq < 2; qq++) {
-            ql[qq] = *(const uint4*)(rq + g * 64 + (2 * h + qq) * 16);
-            qh[qq] = *(const uint4*)(rq + 128 + (2 * h + qq) * 16);
+            ql[qq] = *(const uint4*)(rq + g * 32 + qq * 16);
+            qh[qq] = *(const uint4*)(rq + 64 + qq * 16);
           }
-          if (c == 2) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&raw_empty[rb]);  // the raw block is in registers
+          if (c == 0) {
+            const uint4 sv = *(const uint4*)(raw + rb * RAWH_BYTES + RAWH_Q + row * 16);
+            scw[0] = sv.x, scw[1] = sv.y, scw[2] = sv.z, scw[3] = sv.w;
           }
         }
-        if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1, p.err))) break;
-        uint8_t* arow = smem + s * QSTAGE_BYTES + row * 128;
+        if (round > 0 && !(ok = mbar_wait(&aempty[s], (round - 1) & 1, p.err))) break;
+        uint8_t* arow = smem + s * QA_BYTES + row * 128;
 #pragma unroll
         for (int qq = 0; qq < 2; qq++) {
           const int uu = 2 * h + qq;
@@ -477,9 +477,16 @@ __global__ void __launch_bounds__(QTHREADS, 1)
           *(uint4*)(arow + ((p0 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *(uint4*)(arow + (((p0 + 1) ^ (row & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
+        // The A writes go to the tensor core (async proxy), and for c = 0, 2
+        // the raw half just consumed is refilled by TMA (async proxy) once
+        // released: order this thread's shared-memory accesses first. The raw
+        // loads are complete here (their values fed the A writes).
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[s]);
+        if (lane == 0) {
+          mbar_arrive(&afull[s]);
+          if ((c & 1) == 0) mbar_arrive(&raw_empty[(2 * b + h) & 1]);  // this half is in registers
+        }
         // the previous super-block's accumulator is complete by now: fold it in
         if (c == 1 && b >= 1) epilogue(b - 1, d_fold);
       }
@@ -687,7 +694,7 @@ cudaError_t map_raw(CUtensorMap* mq, CUtensorMap* ms, const Q6Mat& W) {
   {
     const cuuint64_t dims[3] = {(cuuint64_t)U * 16, 3, (cuuint64_t)W.rows};
     const cuuint64_t strides[2] = {(cuuint64_t)U * 16, (cuuint64_t)U * 48};
-    const cuuint32_t box[3] = {64, 3, 128};
+    const cuuint32_t box[3] = {32, 3, 128};  // half a super-block: 2 units x 3 pieces x 128 rows
     const cuuint32_t estr[3] = {1, 1, 1};
     if (fn(mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)W.q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
