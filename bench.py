@@ -274,6 +274,27 @@ def run_reference(args, ws, rank, pg):
     print(json.dumps(line), flush=True)
 
 
+def prefill_only(local: int, n: int) -> dict:
+    """One warm-up and one timed n-token prefill on GPU `local` (device time
+    of the engine's prefill, CUDA events on its stream)."""
+    import torch
+
+    import lfm2_b200
+    torch.cuda.set_device(local)
+    eng = lfm2_b200.GpuEngine(model_path(0, None), local)
+    eng.set_ctx(max(4096, n))
+    p = prompt(n, 11)
+    eng.reset_session()
+    eng.forward(p, 0)
+    eng.reset_session()
+    logits = eng.forward(p, 0)
+    ms = eng.last_device_ms()
+    out = {"prefill_only": n, "ms": round(ms, 3), "tok_s": round(n / (ms / 1000), 1),
+           "argmax": int(np.argmax(logits)), "path": eng.info().get("prefill_path", "")}
+    eng.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -284,12 +305,18 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-micro", action="store_true")
     ap.add_argument("--micro-only", action="store_true", help="only the config-1 Q6_K matvec microbench")
+    ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
+                    help="only one warm-up and one timed N-token prefill (profiling entry point)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local, pg = dist_setup(args.gpus)
     if args.micro_only:
         if rank == 0:
             print(json.dumps({"microbench": microbench(local)}), flush=True)
+        return
+    if args.prefill_only:
+        if rank == 0:
+            print(json.dumps(prefill_only(local, args.prefill_only)), flush=True)
         return
     if args.impl == "reference":
         run_reference(args, ws, rank, pg)

@@ -795,9 +795,9 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
   };
   for (uint32_t l = 0; l < hp.n_layers; l++) {
     const LayerW& L = layers[l];
-    rmsnorm_n(px, L.attn_norm, eps, n, ph, s);
+    if (tc) CK(tc_split_norm(px, L.attn_norm, eps, n, ph, tcs, s));  // RMSNorm + operand split
+    else rmsnorm_n(px, L.attn_norm, eps, n, ph, s);
     nl++;
-    if (tc) split(ph, DIM);
     if (L.attn) {
       const int ld = DIM + 2 * KV_HEADS * HEAD_DIM;
       mm(L.q, ph, pqkv, ld, false);
@@ -825,10 +825,10 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       nl += L.dense ? 2 : 3;
       continue;
     }
-    rmsnorm_n(px, L.ffn_norm, eps, n, ph, s);
+    if (tc && L.dense) CK(tc_split_norm(px, L.ffn_norm, eps, n, ph, tcs, s));
+    else rmsnorm_n(px, L.ffn_norm, eps, n, ph, s);
     nl++;
     if (L.dense) {
-      if (tc) split(ph, DIM);
       mm(L.gate, ph, pgate, N_FF, false);
       mm(L.up, ph, pup, N_FF, false);
       if (tc) {

@@ -289,25 +289,37 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* qkv, const __
   o[lane + 32] = o1 / l;
 }
 
-// Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574):
-// one warp per (token, expert), then route_n picks the top 4.
-__global__ void k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
-  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= n * N_EXPERT) return;
-  const int j = gw / N_EXPERT, e = gw % N_EXPERT;
-  const float4* w = (const float4*)(Wr + (size_t)e * DIM);
-  const float4* x = (const float4*)(xn + (size_t)j * DIM);
-  float a = 0.f;
-  for (int i = lane; i < DIM / 4; i += 32) {
-    const float4 v = w[i], xv = x[i];
-    a = fmaf(v.x, xv.x, a);
-    a = fmaf(v.y, xv.y, a);
-    a = fmaf(v.z, xv.z, a);
-    a = fmaf(v.w, xv.w, a);
+// Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574),
+// then route_n picks the top 4. One block per 32 tokens: 128-wide K chunks of
+// the 32 token rows and the 32 router rows are staged in shared memory and
+// thread (token t / 8, experts t % 8 + 8i) accumulates four dots.
+__global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
+  constexpr int KC = 128;
+  __shared__ float xs[32][KC + 1], ws[N_EXPERT][KC + 1];
+  const int t = threadIdx.x, j0 = blockIdx.x * 32;
+  const int tok = t >> 3, e0 = t & 7;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < DIM; k0 += KC) {
+    for (int f = t; f < 32 * KC / 4; f += 256) {
+      const int r = f / (KC / 4), c4 = f % (KC / 4);
+      const int j = min(j0 + r, n - 1);
+      const float4 xv = *(const float4*)(xn + (size_t)j * DIM + k0 + 4 * c4);
+      const float4 wv = *(const float4*)(Wr + (size_t)r * DIM + k0 + 4 * c4);
+      xs[r][4 * c4] = xv.x, xs[r][4 * c4 + 1] = xv.y, xs[r][4 * c4 + 2] = xv.z, xs[r][4 * c4 + 3] = xv.w;
+      ws[r][4 * c4] = wv.x, ws[r][4 * c4 + 1] = wv.y, ws[r][4 * c4 + 2] = wv.z, ws[r][4 * c4 + 3] = wv.w;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < KC; k++) {
+      const float xv = xs[tok][k];
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[i] = fmaf(ws[e0 + 8 * i][k], xv, acc[i]);
+    }
+    __syncthreads();
   }
-  a = warp_sum(a);
-  if (lane == 0) logits[(size_t)j * N_EXPERT + e] = a;
+  if (j0 + tok < n)
+#pragma unroll
+    for (int i = 0; i < 4; i++) logits[(size_t)(j0 + tok) * N_EXPERT + e0 + 8 * i] = acc[i];
 }
 
 // Stable per-expert slot lists (kernels/persistent.rs:58-76): block e scans
@@ -416,7 +428,8 @@ void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int star
 }
 
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
-  k_router_logits_n<<<(n * N_EXPERT + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
+  static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
+  k_router_logits_n<<<(n + 31) / 32, 256, 0, s>>>(Wr, xnorm, n, logits);
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {

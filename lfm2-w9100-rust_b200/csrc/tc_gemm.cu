@@ -579,6 +579,65 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* u
   if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
 }
 
+// RMSNorm fused with the dense operand split (rows of DIM): the normalised
+// row x * (1 / sqrt(mean(x^2) + eps)) * w is written to `normed` (fp32, the
+// same operations and order as the standalone rmsnorm kernel) and split into
+// the hi/lo operand like k_tc_split.
+__global__ void __launch_bounds__(256) k_tc_split_norm(const float* X, const float* w, float eps, float* normed,
+                                                       int rpad, __half* xg, float* inv) {
+  __shared__ float srow[DIM];
+  __shared__ float red[8];
+  const int r = blockIdx.x;
+  const float* xr = X + (size_t)r * DIM;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < DIM; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < 8; i++) t += red[i];
+  const float rinv = 1.0f / sqrtf(t / (float)DIM + eps);
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < DIM; i += 256) {
+    const float v = xr[i] * rinv * w[i];
+    srow[i] = v;
+    normed[(size_t)r * DIM + i] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  __syncthreads();  // red is reused
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+  int ex = 0;
+  if (mx > 0.f && mx < 3.0e38f) {
+    frexpf(mx, &ex);
+    ex = min(max(14 - ex, -100), 100);
+  } else {
+    ex = 0;
+  }
+  const float sc = ldexpf(1.f, ex);
+  __half* hi = xg + (size_t)r * DIM;
+  __half* lo = xg + ((size_t)rpad + r) * DIM;
+  for (int k = threadIdx.x * 4; k < DIM; k += 1024) {
+    __half h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float f = srow[k + j] * sc;
+      h[j] = __float2half_rn(f);
+      l[j] = __float2half_rn(f - __half2float(h[j]));
+    }
+    const __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+    const __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+    *(uint2*)(hi + k) = make_uint2(*(const uint32_t*)&h01, *(const uint32_t*)&h23);
+    *(uint2*)(lo + k) = make_uint2(*(const uint32_t*)&l01, *(const uint32_t*)&l23);
+  }
+  if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
+}
+
 // Grouped layout from the expert lists (groups[e * (cap + 1)] = count, then
 // the selection slots): experts' rows start at 128-aligned bases; tiles =
 // {count, (expert, first row) ...}; slots[row] = selection slot or -1;
@@ -745,6 +804,14 @@ cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc,
   const int rpad = dense_rpad(n);
   if (n <= 0 || K % 64 || K > TC_SPLIT_KMAX || ldx % 4 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
   k_tc_split<<<n, 256, K * 4, s>>>(X, up, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_split_norm(const float* X, const float* w, float eps, int n, float* normed, const TcScratch& sc,
+                          cudaStream_t s) {
+  const int rpad = dense_rpad(n);
+  if (n <= 0 || !fits(sc, rpad, DIM)) return cudaErrorInvalidValue;
+  k_tc_split_norm<<<n, 256, 0, s>>>(X, w, eps, normed, rpad, sc.xg, sc.inv);
   return cudaGetLastError();
 }
 

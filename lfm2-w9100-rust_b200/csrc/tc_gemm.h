@@ -55,6 +55,10 @@ bool tc_q6_supported(const Q6Mat& W, int out_rows);
 constexpr int TC_SPLIT_KMAX = 12288;  // row length held in shared memory
 cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s,
                      const float* up = nullptr);
+// RMSNorm of rows [0, n) of X [n][2048] with weights w into `normed` (fp32),
+// fused with the split of the normalised rows into the operand.
+cudaError_t tc_split_norm(const float* X, const float* w, float eps, int n, float* normed, const TcScratch& sc,
+                          cudaStream_t s);
 cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
                        cudaStream_t s);
 
