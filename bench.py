@@ -274,6 +274,60 @@ def run_reference(args, ws, rank, pg):
     print(json.dumps(line), flush=True)
 
 
+SESSIONS, SESSION_GEN = 64, 128
+
+
+def multi_session(eng, peaks, pg, ws: int, info: dict) -> dict:
+    """Config 4 on this GPU: 64 independent sessions with seeded prompt lengths
+    uniform in [128, 1024] and seeded token ids, each prefilled on its own,
+    then 128 greedy tokens for all of them in batched steps (one token per
+    session per step). Device time per call (CUDA events), max over ranks;
+    aggregate = all ranks' tokens / that time. The HBM roofline of a batched
+    step counts every weight once (64 tokens x top-4 of 32 experts touch all
+    experts) plus each session's K/V read."""
+    rng = np.random.default_rng(21)
+    lens = rng.integers(128, 1025, SESSIONS)
+    prompts = [rng.integers(0, VOCAB, int(n)).astype(np.uint32) for n in lens]
+    eng.batch_create(SESSIONS)
+    sess = np.arange(SESSIONS, dtype=np.uint32)
+    # warm-up: one prefill and two batched steps (first-touch, module load)
+    t = eng.batch_prefill(0, prompts[0][:64])
+    eng.batch_decode(sess[:1], [t], [64])
+    eng.batch_decode(sess, np.ones(SESSIONS, np.uint32), np.zeros(SESSIONS, np.uint32))
+    barrier(pg)
+    pf_ms, toks = 0.0, []
+    w0 = time.perf_counter()
+    for i, p in enumerate(prompts):
+        toks.append(eng.batch_prefill(i, p))
+        pf_ms += eng.last_device_ms()
+    toks = np.array(toks, np.uint32)
+    pos = lens.astype(np.uint32).copy()
+    dec_ms = 0.0
+    w1 = time.perf_counter()
+    for _ in range(SESSION_GEN):
+        toks = eng.batch_decode(sess, toks, pos)
+        dec_ms += eng.last_device_ms()
+        pos += 1
+    w2 = time.perf_counter()
+    dec_max = reduce_max(pg, dec_ms)
+    pf_max = reduce_max(pg, pf_ms)
+    wall_dec = reduce_max(pg, w2 - w1)
+    wall_all = reduce_max(pg, w2 - w0)
+    gen = ws * SESSIONS * SESSION_GEN
+    kv = sum(6 * 2 * 8 * 64 * 2 * (int(n) + SESSION_GEN / 2.0) for n in lens)  # fp16 K+V per step, mean ctx
+    step_bytes = info["weight_bytes"] + kv
+    step_s = dec_max / 1000.0 / SESSION_GEN
+    return {"workload": "config 4: 64 sessions/GPU, prompts U[128,1024], 128 greedy tokens each, batched decode",
+            "sessions_per_gpu": SESSIONS, "gen_per_session": SESSION_GEN,
+            "decode_tok_s": round(gen / (dec_max / 1000.0), 1),
+            "decode_ms_per_step": round(dec_max / SESSION_GEN, 3),
+            "prefill_tok_s": round(ws * float(lens.sum()) / (pf_max / 1000.0), 1),
+            "e2e_tok_s": round(gen / wall_all, 1), "e2e_decode_tok_s": round(gen / wall_dec, 1),
+            "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                         "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4)}}
+
+
 def prefill_only(local: int, n: int) -> dict:
     """One warm-up and one timed n-token prefill on GPU `local` (device time
     of the engine's prefill, CUDA events on its stream)."""
@@ -305,6 +359,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-micro", action="store_true")
     ap.add_argument("--micro-only", action="store_true", help="only the config-1 Q6_K matvec microbench")
+    ap.add_argument("--no-sessions", action="store_true", help="skip config 4 (64 independent sessions per GPU)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
                     help="only one warm-up and one timed N-token prefill (profiling entry point)")
     args = ap.parse_args()
@@ -400,6 +455,9 @@ def main():
                    "ms": round(pms, 2), "tflops": round(fl / (pms / 1000) / 1e12, 2),
                    "frac_of_bf16_peak": round(fl / (pms / 1000) / 1e12 / peaks["bf16_tflops"], 4),
                    "path": info.get("prefill_path", "")}
+    multi = None
+    if not args.no_sessions:
+        multi = multi_session(eng, peaks, pg, ws, info)
     micro = None
     if rank == 0 and not args.no_micro:
         micro = microbench(local)
@@ -417,7 +475,7 @@ def main():
                            "decode_path": path_name,
                            "l2": "no flush needed: every step streams ~1.4 GB of weights (> 126 MB L2)"},
                 "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk.summary(), "prefill": prefill, "microbench": micro, "cpu_baseline": cpu,
+                "clocks": clk.summary(), "prefill": prefill, "multi_session": multi, "microbench": micro, "cpu_baseline": cpu,
                 "tokens_head": toks[:8]}
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -117,6 +117,27 @@ lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_p
 /* CUDA-event device time (ms) of the last forward / decode call. */
 float lfm_last_device_ms(lfm_engine* e);
 
+/* Independent sessions decoded together (multi-session throughput). The
+ * reference serves one session at a time and switches sessions by
+ * snapshot/restore of its single buffer set (persistent.rs:164-176,
+ * resident_graph.rs:572-602); here each session slot owns a KV cache and a
+ * conv state at the engine's current context length, and one batched step
+ * advances many sessions at once (every weight is read once per step).
+ * lfm_batch_create: n_sessions slots (1..4096), replacing earlier ones. */
+lfm_status lfm_batch_create(lfm_engine* e, uint32_t n_sessions);
+/* Fresh prompt of session `session` at positions 0..n-1 (its conv state is
+ * reset first, like reset_session); *next_token = greedy next token. */
+lfm_status lfm_batch_prefill(lfm_engine* e, uint32_t session, const uint32_t* ids, uint32_t n,
+                             uint32_t* next_token);
+/* One decode step of `count` distinct sessions: token tokens[i] at position
+ * positions[i] of session sessions[i]; next_tokens[i] = greedy next token
+ * (forward_token semantics per session, resident_graph.rs:90-101). */
+lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint32_t* tokens,
+                            const uint32_t* positions, uint32_t count, uint32_t* next_tokens);
+/* Full logits (vocab floats) of entry `index` of the last lfm_batch_decode
+ * step (snapshot_resident_logits, resident_graph.rs:561-568, for one batch entry). */
+lfm_status lfm_batch_logits(lfm_engine* e, uint32_t index, float* logits);
+
 /* Per-stage timeline of the persistent decode step, for profiling (the
  * reference's per-dispatch GPU timestamp queries, vulkan/profile.rs:18-45,
  * enabled by LFM_PROFILE_DISPATCH). `enable`

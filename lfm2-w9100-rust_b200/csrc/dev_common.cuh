@@ -56,8 +56,20 @@ struct WaitBudget {
     return now - t0 > WAIT_CYCLES;
   }
 };
+// Non-blocking probe of a phase (no suspend): the cheap path when the phase
+// has usually completed already.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: false after ~1 s without completion (error word raised).
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, unsigned* err) {
+  if (mbar_test_wait(b, parity)) return true;
   WaitBudget wb;
   for (uint32_t i = 0;; i++) {
     if (mbar_try_wait(b, parity)) return true;

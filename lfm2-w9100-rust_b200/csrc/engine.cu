@@ -66,6 +66,33 @@ struct CudaError {
     if (_e != cudaSuccess) throw ::lfm::CudaError{_e}; \
   } while (0)
 
+// Per-token session map of a batched decode step: token j is at position
+// pos[j] of session sess[j]; sessions' caches and conv states lie kv_stride /
+// conv_stride elements apart, starting at session 0's.
+struct TokBatch {
+  const int* pos = nullptr;
+  const int* sess = nullptr;
+  __half* kc = nullptr;
+  __half* vc = nullptr;
+  float* conv = nullptr;
+  size_t kv_stride = 0, conv_stride = 0;
+  float* part = nullptr;  // attention split partials
+};
+
+// Device state of the independent sessions (lfm_batch_*).
+struct BatchState {
+  uint32_t nsess = 0, ctx = 0;
+  __half *kc = nullptr, *vc = nullptr;  // [session][attn layer][kv head][ctx][64]
+  float* conv = nullptr;                // [session][conv layer][2048][2]
+  size_t kv_stride = 0, conv_stride = 0;
+  int* map = nullptr;                   // per step: tokens | positions | sessions
+  int* next = nullptr;
+  float* logits = nullptr;              // [session][vocab]
+  float* attn_part = nullptr;           // attention split partials of one step
+  std::vector<int> h_map;
+  std::vector<void*> allocs;
+};
+
 }  // namespace
 
 struct EngineImpl {
@@ -138,6 +165,7 @@ struct EngineImpl {
     if (ev1) cudaEventDestroy(ev1);
     free_prefill();
     free_state();
+    batch_free();
     for (void* p : weight_allocs) cudaFree(p);
     if (h_io) cudaFreeHost(h_io);
     if (stream) cudaStreamDestroy(stream);
@@ -192,6 +220,13 @@ struct EngineImpl {
   void check_device_error();
   void run_decode(uint32_t token, uint32_t pos);
   void run_prefill(const uint32_t* ids, int n, uint32_t start);
+  void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl);
+  BatchState batch;
+  void batch_create(uint32_t nsess);
+  void batch_free();
+  uint32_t batch_prefill(uint32_t sess, const uint32_t* ids, int n);
+  void run_batch_decode(uint32_t count, const uint32_t* tokens, const uint32_t* pos, const uint32_t* sess,
+                        uint32_t* next);
   void run_loop(uint32_t steps, uint32_t* out_tokens);
   std::vector<uint8_t> snapshot(uint32_t valid);
   void restore(uint32_t valid, const uint8_t* buf, size_t len);
@@ -549,9 +584,11 @@ void EngineImpl::ensure_prefill(int n) {
   tcs.halves = std::max<size_t>(2 * ((N + 127) / 128 * 128) * N_FF, 2 * tcs.rows * DIM);
   tcs.xg = dalloc<__half>(prefill_allocs, tcs.halves);
   tcs.inv = dalloc<float>(prefill_allocs, tcs.rows);
-  tcs.tiles = dalloc<int>(prefill_allocs, 1 + 2 * (size_t)tc_max_tiles(cap));
+  tcs.tiles = dalloc<int>(prefill_allocs, 1 + 2 * (size_t)tc_max_tiles_cap(cap));
   tcs.slots = dalloc<int>(prefill_allocs, tcs.rows);
   tcs.rowof = dalloc<int>(prefill_allocs, N * N_USED);
+  tcs.part_cap = (size_t)16 * std::min<size_t>(N, 128) * N_FF;  // split-K partials of one token tile
+  tcs.part = dalloc<float>(prefill_allocs, tcs.part_cap);
   ncap = cap;
 }
 
@@ -767,15 +804,16 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
 }
 
 // n > 1 tokens starting at `start` (resident_graph.rs:226-551 with n columns).
-void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
-  ensure_prefill(n);
+// The layer stack over n token rows in px (embedded), leaving the final
+// residual stream in px. tb == nullptr: consecutive prompt tokens of the
+// current session at positions start..start+n-1 (its caches kc/vc and conv
+// state), with the last layer's FFN on the last token only (lfm.rs:540-541).
+// tb != nullptr: one token from each of n independent sessions (batched
+// decode): positions, sessions and per-session caches come from tb, and every
+// token runs every layer.
+void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl) {
   cudaStream_t s = stream;
   const float eps = hp.eps;
-  int nl = 0;
-  CK(cudaEventRecord(ev0, s));
-  CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-  embed_n(embd, pids, n, px, s);
-  nl++;
   LaunchCfg c;
   c.stream = s;
   c.pdl = false;
@@ -803,23 +841,30 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       mm(L.q, ph, pqkv, ld, false);
       mm(L.k, ph, pqkv + DIM, ld, false);
       mm(L.v, ph, pqkv + DIM + KV_HEADS * HEAD_DIM, ld, false);
-      __half* kcl = kc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
-      __half* vcl = vc + (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
-      qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kcl, vcl, s);
-      if (tc) CK(attn_prefill_tc(pqkv, ld, kcl, vcl, (int)start, n, (int)ctx, pa, DIM, tcs.err, s));
-      else attn_prefill(pqkv, kcl, vcl, start, n, ctx, pa, s);
+      const size_t loff = (size_t)L.attn_idx * KV_HEADS * ctx * HEAD_DIM;
+      if (tb) {
+        qk_prep_batch(pqkv, L.q_norm, L.k_norm, rope, n, ctx, eps, tb->kc + loff, tb->vc + loff, tb->pos, tb->sess,
+                      tb->kv_stride, s);
+        attn_batch(pqkv, tb->kc + loff, tb->vc + loff, n, ctx, pa, tb->pos, tb->sess, tb->kv_stride, tb->part, s);
+      } else {
+        qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kc + loff, vc + loff, s);
+        if (tc) CK(attn_prefill_tc(pqkv, ld, kc + loff, vc + loff, (int)start, n, (int)ctx, pa, DIM, tcs.err, s));
+        else attn_prefill(pqkv, kc + loff, vc + loff, start, n, ctx, pa, s);
+      }
       if (tc) split(pa, DIM);
       mm(L.o, pa, px, DIM, true);
       nl += 2;
     } else {
       mm(L.in_proj, ph, pbcx, 3 * DIM, false);
-      conv_prefill(pbcx, L.conv_w, conv_state + (size_t)L.conv_idx * DIM * 2, n, pgated, s);
+      const size_t coff = (size_t)L.conv_idx * DIM * 2;
+      if (tb) conv_batch(pbcx, L.conv_w, tb->conv + coff, tb->conv_stride, tb->sess, n, pgated, s);
+      else conv_prefill(pbcx, L.conv_w, conv_state + coff, n, pgated, s);
       if (tc) split(pgated, DIM);
       mm(L.out_proj, pgated, px, DIM, true);
-      nl += 2;
+      nl += tb ? 1 : 2;
     }
     const bool last = l == hp.n_layers - 1;
-    if (last) {
+    if (last && !tb) {
       // The last layer's FFN only runs on the last token (lfm.rs:540-541).
       enqueue_ffn(L, px + (size_t)(n - 1) * DIM, c, (unsigned*)(io + 4));
       nl += L.dense ? 2 : 3;
@@ -861,6 +906,22 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
       ctr.expert_grouped_launches += 3;
     }
   }
+}
+
+void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
+  ensure_prefill(n);
+  cudaStream_t s = stream;
+  const float eps = hp.eps;
+  int nl = 0;
+  CK(cudaEventRecord(ev0, s));
+  CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  embed_n(embd, pids, n, px, s);
+  nl++;
+  enqueue_layers(n, start, nullptr, nl);
+  LaunchCfg c;
+  c.stream = s;
+  c.pdl = false;
+  c.sms = sms;
   if (use_mvt)
     mvt_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2,
                (unsigned*)(io + 4), c);
@@ -875,6 +936,108 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
   ctr.kernel_launches += nl;
   ctr.gpu_argmax++;
   ctr.prefill_tokens += n;
+  check_device_error();
+}
+
+// ---------------------------------------------------------------- sessions
+// Independent sessions with their own KV caches and conv states, prefilled one
+// at a time and decoded together, one token per session per step (the
+// reference time-multiplexes sessions by snapshot/restore through one set of
+// buffers, persistent.rs:164-176).
+void EngineImpl::batch_create(uint32_t nsess) {
+  ensure_state();
+  batch_free();
+  BatchState& B = batch;
+  B.nsess = nsess;
+  B.ctx = ctx;
+  B.kv_stride = (size_t)std::max(n_attn, 1) * KV_HEADS * ctx * HEAD_DIM;
+  B.conv_stride = (size_t)std::max(n_conv, 1) * DIM * 2;
+  B.kc = dalloc<__half>(B.allocs, B.kv_stride * nsess);
+  B.vc = dalloc<__half>(B.allocs, B.kv_stride * nsess);
+  B.conv = dalloc<float>(B.allocs, B.conv_stride * nsess);
+  CK(cudaMemsetAsync(B.kc, 0, B.kv_stride * nsess * 2, stream));
+  CK(cudaMemsetAsync(B.vc, 0, B.kv_stride * nsess * 2, stream));
+  CK(cudaMemsetAsync(B.conv, 0, B.conv_stride * nsess * 4, stream));
+  B.map = dalloc<int>(B.allocs, 3 * (size_t)nsess);  // tokens | positions | sessions
+  B.next = dalloc<int>(B.allocs, nsess);
+  B.logits = dalloc<float>(B.allocs, (size_t)nsess * hp.vocab);
+  B.attn_part = dalloc<float>(B.allocs, attn_batch_part_floats((int)nsess, (int)ctx));
+  B.h_map.resize(3 * (size_t)nsess);
+  CK(cudaStreamSynchronize(stream));
+}
+
+void EngineImpl::batch_free() {
+  for (void* p : batch.allocs) cudaFree(p);
+  batch = BatchState();
+}
+
+// Prefill session `sess` with its prompt (positions 0..n-1): the single-session
+// prompt path with the session's caches in place of the engine's own.
+uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n) {
+  BatchState& B = batch;
+  __half* k0 = kc;
+  __half* v0 = vc;
+  float* c0 = conv_state;
+  kc = B.kc + (size_t)sess * B.kv_stride;
+  vc = B.vc + (size_t)sess * B.kv_stride;
+  conv_state = B.conv + (size_t)sess * B.conv_stride;
+  CK(cudaMemsetAsync(conv_state, 0, B.conv_stride * 4, stream));  // a fresh session (reset_session)
+  try {
+    run_prefill(ids, n, 0);
+  } catch (...) {
+    kc = k0, vc = v0, conv_state = c0;
+    throw;
+  }
+  kc = k0, vc = v0, conv_state = c0;
+  return (uint32_t)h_io[2];
+}
+
+// One decode step of `count` sessions: token tokens[i] at position pos[i] of
+// session sess[i] (distinct sessions); next[i] = greedy next token.
+void EngineImpl::run_batch_decode(uint32_t count, const uint32_t* tokens, const uint32_t* pos, const uint32_t* sess,
+                                  uint32_t* next) {
+  BatchState& B = batch;
+  const int n = (int)count;
+  ensure_prefill(n);
+  cudaStream_t s = stream;
+  const float eps = hp.eps;
+  int nl = 0;
+  for (int i = 0; i < n; i++) {
+    B.h_map[i] = (int)tokens[i];
+    B.h_map[n + i] = (int)pos[i];
+    B.h_map[2 * n + i] = (int)sess[i];
+  }
+  CK(cudaEventRecord(ev0, s));
+  CK(cudaMemcpyAsync(B.map, B.h_map.data(), (size_t)3 * n * 4, cudaMemcpyHostToDevice, s));
+  embed_n(embd, (const uint32_t*)B.map, n, px, s);
+  nl++;
+  TokBatch tb;
+  tb.pos = B.map + n;
+  tb.sess = B.map + 2 * n;
+  tb.kc = B.kc;
+  tb.vc = B.vc;
+  tb.conv = B.conv;
+  tb.kv_stride = B.kv_stride;
+  tb.conv_stride = B.conv_stride;
+  tb.part = B.attn_part;
+  enqueue_layers(n, 0, &tb, nl);
+  // final norm + tied lm_head for every token, then the row argmax
+  if (use_tc && n >= tc_min) {
+    CK(tc_split_norm(px, out_norm, eps, n, ph, tcs, s));
+    CK(tc_gemm_q6(embd, n, B.logits, (int)hp.vocab, false, tcs, s));
+  } else {
+    rmsnorm_n(px, out_norm, eps, n, ph, s);
+    gemm_q6_ld(embd, ph, n, B.logits, (int)hp.vocab, false, s);
+  }
+  argmax_rows(B.logits, n, (int)hp.vocab, B.next, s);
+  nl += 3;
+  CK(cudaMemcpyAsync(next, B.next, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(ev1, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaGetLastError());
+  CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  ctr.kernel_launches += nl;
   check_device_error();
 }
 
@@ -1146,6 +1309,80 @@ lfm_status lfm_decode_loop(lfm_engine* e, uint32_t first_token, uint32_t start_p
     float first_ms = I.last_ms;
     if (steps > 1) I.run_loop(steps - 1, out_tokens + 1);
     if (device_ms) *device_ms = steps > 1 ? I.last_ms : first_ms;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_batch_create(lfm_engine* e, uint32_t n_sessions) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (n_sessions == 0 || n_sessions > 4096) {
+      lfm::set_err(&I, "n_sessions must be 1..4096");
+      return LFM_ERR_ARG;
+    }
+    I.batch_create(n_sessions);
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_batch_prefill(lfm_engine* e, uint32_t session, const uint32_t* ids, uint32_t n,
+                             uint32_t* next_token) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (I.batch.nsess == 0 || I.batch.ctx != I.ctx) {
+      lfm::set_err(&I, "no session slots for the current context length (lfm_batch_create)");
+      return LFM_ERR_ARG;
+    }
+    if (session >= I.batch.nsess) {
+      lfm::set_err(&I, "session out of range");
+      return LFM_ERR_ARG;
+    }
+    lfm_status st = check_ids(e, ids, n, 0);
+    if (st) return st;
+    const uint32_t t = I.batch_prefill(session, ids, (int)n);
+    if (next_token) *next_token = t;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint32_t* tokens,
+                            const uint32_t* positions, uint32_t count, uint32_t* next_tokens) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (I.batch.nsess == 0 || I.batch.ctx != I.ctx) {
+      lfm::set_err(&I, "no session slots for the current context length (lfm_batch_create)");
+      return LFM_ERR_ARG;
+    }
+    if (!sessions || !tokens || !positions || !next_tokens || count == 0 || count > I.batch.nsess) {
+      lfm::set_err(&I, "batch decode: bad arguments");
+      return LFM_ERR_ARG;
+    }
+    std::vector<uint8_t> seen(I.batch.nsess, 0);
+    for (uint32_t i = 0; i < count; i++) {
+      if (sessions[i] >= I.batch.nsess || seen[sessions[i]]) {
+        lfm::set_err(&I, "batch decode: sessions must be distinct and in range");
+        return LFM_ERR_ARG;
+      }
+      seen[sessions[i]] = 1;
+      if (tokens[i] >= I.hp.vocab || positions[i] >= I.ctx) {
+        lfm::set_err(&I, "batch decode: token or position out of range");
+        return LFM_ERR_ARG;
+      }
+    }
+    I.run_batch_decode(count, tokens, positions, sessions, next_tokens);
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_batch_logits(lfm_engine* e, uint32_t index, float* logits) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!logits || I.batch.nsess == 0 || index >= I.batch.nsess) {
+      lfm::set_err(&I, "batch logits: bad arguments");
+      return LFM_ERR_ARG;
+    }
+    CK(cudaMemcpy(logits, I.batch.logits + (size_t)index * I.hp.vocab, (size_t)I.hp.vocab * 4,
+                  cudaMemcpyDeviceToHost));
     return LFM_OK;
   });
 }

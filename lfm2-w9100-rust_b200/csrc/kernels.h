@@ -137,6 +137,19 @@ void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float
                int start, int n, int ctx, float eps, __half* kc, __half* vc, cudaStream_t s);
 void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int start, int n, int ctx,
                   float* out, cudaStream_t s);
+// Batched decode of independent sessions: token j is at position tpos[j] of
+// session tsess[j]; per-session caches / conv states lie sstride elements apart.
+void qk_prep_batch(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int n, int ctx,
+                   float eps, __half* kc, __half* vc, const int* tpos, const int* tsess, size_t sstride,
+                   cudaStream_t s);
+// (split over 64-position blocks; `part` holds attn_batch_part_floats(n, ctx) floats)
+size_t attn_batch_part_floats(int n, int ctx);
+void attn_batch(const float* qkv, const __half* kc, const __half* vc, int n, int ctx, float* out, const int* tpos,
+                const int* tsess, size_t sstride, float* part, cudaStream_t s);
+void conv_batch(const float* bcx, const float* conv_w, float* state, size_t sstride, const int* tsess, int n,
+                float* gated, cudaStream_t s);
+// out[i] = argmax of row i of x [n][len].
+void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s);
 // Router logits [n][32] of normalised tokens (f32_matmul, kernels.rs:552-574).
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s);
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s);

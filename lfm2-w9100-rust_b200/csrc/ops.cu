@@ -146,7 +146,8 @@ struct CallScratch {
     sc.rows = rows;
     sc.halves = 2 * rows * K;
     const size_t tiles = 1 + 2 * (rows / 128 + 64);
-    const size_t bytes = sc.halves * 2 + rows * 4 + tiles * 4 + rows * 4 + slots * 4 + 256 * 5;
+    sc.part_cap = rows <= 128 ? (size_t)16 * 128 * 8192 : 0;  // split-K partials (one token tile)
+    const size_t bytes = sc.halves * 2 + rows * 4 + tiles * 4 + rows * 4 + slots * 4 + sc.part_cap * 4 + 256 * 6;
     cudaError_t e = cudaMallocAsync(&mem, bytes, s);
     if (e != cudaSuccess) return e;
     char* p = (char*)mem;
@@ -160,6 +161,7 @@ struct CallScratch {
     sc.tiles = (int*)take(tiles * 4);
     sc.slots = (int*)take(rows * 4);
     sc.rowof = (int*)take(slots * 4);
+    sc.part = sc.part_cap ? (float*)take(sc.part_cap * 4) : nullptr;
     return cudaGetSymbolAddress((void**)&sc.err, g_tc_err);
   }
   // zero the status word, run, read it back; frees the scratch

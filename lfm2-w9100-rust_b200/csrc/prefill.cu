@@ -27,6 +27,10 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+// argmax order: larger value, then smaller index (NaN never wins)
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
 
 // GROUPED = false: columns are tokens 0..n-1, X row j, output row j.
 // GROUPED = true : blockIdx.z = expert; columns are that expert's slots.
@@ -195,13 +199,20 @@ __global__ void k_conv_state(const float* bcx, float* state, int n) {
 }
 
 // Head RMSNorm + NEOX RoPE of q (32 heads) and k (8 heads) in place, then the
-// fp16 K/V cache write at positions start..start+n-1 (lfm.rs:368-393).
+// fp16 K/V cache write at positions start..start+n-1 (lfm.rs:368-393). With a
+// token map (batched decode of independent sessions), token j is at position
+// tpos[j] of session tsess[j], whose caches start sstride elements apart.
 __global__ void k_qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope,
-                            int start, int ctx, float eps, __half* kc, __half* vc) {
+                            int start, int ctx, float eps, __half* kc, __half* vc, const int* tpos,
+                            const int* tsess, size_t sstride) {
   const int j = blockIdx.x;
   const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);  // 0..47
   const int lane = threadIdx.x & 31;
-  const int pos = start + j;
+  const int pos = tpos ? tpos[j] : start + j;
+  if (tsess) {
+    kc += (size_t)tsess[j] * sstride;
+    vc += (size_t)tsess[j] * sstride;
+  }
   float* row = qkv + (size_t)j * (DIM + 2 * KV_HEADS * HEAD_DIM);
   if (hh < HEADS + KV_HEADS) {
     const bool isq = hh < HEADS;
@@ -234,14 +245,19 @@ __global__ void k_qk_prep_n(float* qkv, const float* q_norm, const float* k_norm
 // Causal GQA attention for n new tokens over the fp16 cache (lfm.rs:395-437):
 // one warp per (token, head), online softmax over 32-position chunks.
 __global__ void __launch_bounds__(256) k_attn_prefill(const float* qkv, const __half* kc, const __half* vc,
-                                                      int start, int n, int ctx, float* out) {
+                                                      int start, int n, int ctx, float* out, const int* tpos,
+                                                      const int* tsess, size_t sstride) {
   __shared__ float sq[8][HEAD_DIM];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 8 + warp;
   if (gw >= n * HEADS) return;
   const int j = gw / HEADS, h = gw % HEADS;
   const int kh = h / (HEADS / KV_HEADS);
-  const int p = start + j;
+  const int p = tpos ? tpos[j] : start + j;
+  if (tsess) {
+    kc += (size_t)tsess[j] * sstride;
+    vc += (size_t)tsess[j] * sstride;
+  }
   const float* q = qkv + (size_t)j * (DIM + 2 * KV_HEADS * HEAD_DIM) + h * HEAD_DIM;
   sq[warp][lane] = q[lane];
   sq[warp][lane + 32] = q[lane + 32];
@@ -289,37 +305,198 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* qkv, const __
   o[lane + 32] = o1 / l;
 }
 
+// Decode attention of one token per session (batched decode; lfm.rs:395-437
+// for one query): block (kv head, split, token) scores the 64 cached
+// positions of its split for the 4 query heads of the KV head (one warp each,
+// two positions per lane) and leaves a partial (max, sum, weighted V) that
+// k_attn_batch_merge combines over the token's splits in order. q is already
+// head-normalised and rotated (k_qk_prep_n); the split holding the token's
+// own position reads the K/V row that k_qk_prep_n wrote.
+constexpr int ABS = 64;  // positions per split
+__global__ void __launch_bounds__(128) k_attn_batch(const float* qkv, const __half* kc, const __half* vc, int ctx,
+                                                    const int* tpos, const int* tsess, size_t sstride, float* part,
+                                                    int nsplit_max) {
+  constexpr int KP = HEAD_DIM + 8;
+  __shared__ float sq[4][HEAD_DIM];
+  __shared__ __align__(16) __half sk[ABS][KP];
+  __shared__ __align__(16) __half sv[ABS][HEAD_DIM];
+  const int kh = blockIdx.x, split = blockIdx.y, j = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = tpos[j];
+  const int t0 = split * ABS;
+  if (t0 > pos) return;
+  const size_t sbase = (size_t)tsess[j] * sstride;
+  const int h = kh * (HEADS / KV_HEADS) + warp;
+  const float* q = qkv + (size_t)j * (DIM + 2 * KV_HEADS * HEAD_DIM) + h * HEAD_DIM;
+  sq[warp][lane] = q[lane];
+  sq[warp][lane + 32] = q[lane + 32];
+  const int cnt = min(ABS, pos + 1 - t0);
+  {
+    const uint4* kg = (const uint4*)(kc + sbase + ((size_t)kh * ctx + t0) * HEAD_DIM);
+    const uint4* vg = (const uint4*)(vc + sbase + ((size_t)kh * ctx + t0) * HEAD_DIM);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int idx = threadIdx.x + i * 128;  // 0..511 = 64 rows x 8 pieces
+      const int r = idx >> 3, c = idx & 7;
+      if (r < cnt) {
+        *(uint4*)&sk[r][c * 8] = kg[idx];
+        *(uint4*)&sv[r][c * 8] = vg[idx];
+      }
+    }
+  }
+  __syncthreads();
+  float sc[2];
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    const int r = lane + 32 * hf;
+    sc[hf] = -INFINITY;
+    if (r < cnt) {
+      float acc = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; c8++) {
+        const uint4 v = *(const uint4*)&sk[r][c8 * 8];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const float2 f = __half22float2(*(const __half2*)&w[jj]);
+          acc = fmaf(f.x, sq[warp][c8 * 8 + 2 * jj], acc);
+          acc = fmaf(f.y, sq[warp][c8 * 8 + 2 * jj + 1], acc);
+        }
+      }
+      sc[hf] = acc * 0.125f;
+    }
+  }
+  const float m = warp_max(fmaxf(sc[0], sc[1]));
+  const float p0 = lane < cnt ? expf(sc[0] - m) : 0.f;
+  const float p1 = lane + 32 < cnt ? expf(sc[1] - m) : 0.f;
+  const float l = warp_sum(p0 + p1);
+  float o0 = 0.f, o1 = 0.f;
+  for (int t = 0; t < cnt; t++) {
+    const float pt = __shfl_sync(0xffffffffu, t < 32 ? p0 : p1, t & 31);
+    o0 = fmaf(pt, __half2float(sv[t][lane]), o0);
+    o1 = fmaf(pt, __half2float(sv[t][lane + 32]), o1);
+  }
+  float* pp = part + ((((size_t)j * KV_HEADS + kh) * nsplit_max + split) * 4 + warp) * (HEAD_DIM + 2);
+  pp[lane] = o0;
+  pp[lane + 32] = o1;
+  if (lane == 0) {
+    pp[HEAD_DIM] = m;
+    pp[HEAD_DIM + 1] = l;
+  }
+}
+
+// out[j][h*64 + d] = sum_s exp(m_s - M) o_s[d] / sum_s exp(m_s - M) l_s over
+// token j's splits in order; block per token, warp per query head.
+__global__ void __launch_bounds__(1024) k_attn_batch_merge(const float* part, const int* tpos, int nsplit_max,
+                                                           float* out) {
+  const int j = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kh = h / (HEADS / KV_HEADS), w = h % (HEADS / KV_HEADS);
+  const int nact = tpos[j] / ABS + 1;
+  const float* pb = part + (((size_t)j * KV_HEADS + kh) * nsplit_max * 4 + w) * (HEAD_DIM + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nact; s++) M = fmaxf(M, pb[(size_t)s * 4 * (HEAD_DIM + 2) + HEAD_DIM]);
+  float L = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int s = 0; s < nact; s++) {
+    const float* ps = pb + (size_t)s * 4 * (HEAD_DIM + 2);
+    const float f = expf(ps[HEAD_DIM] - M);
+    L = fmaf(ps[HEAD_DIM + 1], f, L);
+    o0 = fmaf(ps[lane], f, o0);
+    o1 = fmaf(ps[lane + 32], f, o1);
+  }
+  float* o = out + (size_t)j * DIM + h * HEAD_DIM;
+  o[lane] = o0 / L;
+  o[lane + 32] = o1 / L;
+}
+
+// Short conv of one token per session (batched decode): token j advances the
+// conv state of its session tsess[j] by one step (kernels/resident.rs:33-56).
+__global__ void k_conv_batch(const float* bcx, const float* conv_w, float* state, size_t sstride, const int* tsess,
+                             int n, float* gated) {
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  const int j = blockIdx.y;
+  if (ch >= DIM || j >= n) return;
+  float* st = state + (size_t)tsess[j] * sstride;
+  const float* r = bcx + (size_t)j * 3 * DIM;
+  const float bx = r[ch] * r[2 * DIM + ch];
+  const float s0 = st[2 * ch], s1 = st[2 * ch + 1];
+  float conv = 0.f;
+  conv += s0 * conv_w[3 * ch];
+  conv += s1 * conv_w[3 * ch + 1];
+  conv += bx * conv_w[3 * ch + 2];
+  gated[(size_t)j * DIM + ch] = r[DIM + ch] * conv;
+  st[2 * ch] = s1;
+  st[2 * ch + 1] = bx;
+}
+
+// Row-wise argmax of [n][len] logits (the reference's GPU argmax semantics:
+// largest value, first index on ties, NaN never selected; main.rs:287-317).
+__global__ void __launch_bounds__(1024) k_argmax_rows(const float* x, int len, int* out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const float* r = x + (size_t)blockIdx.x * len;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < len; i += blockDim.x)
+    if (am_better(r[i], i, bv, bi)) {
+      bv = r[i];
+      bi = i;
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (am_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    bv = threadIdx.x < blockDim.x / 32 ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < blockDim.x / 32 ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (am_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
 // Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574),
-// then route_n picks the top 4. One block per 32 tokens: 128-wide K chunks of
-// the 32 token rows and the 32 router rows are staged in shared memory and
-// thread (token t / 8, experts t % 8 + 8i) accumulates four dots.
+// then route_n picks the top 4. One block per 8 tokens: 128-wide K chunks of
+// the token rows and the 32 router rows are staged in shared memory, and
+// thread (token t / 32, expert t % 32) accumulates its dot in K order.
 __global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
-  constexpr int KC = 128;
-  __shared__ float xs[32][KC + 1], ws[N_EXPERT][KC + 1];
-  const int t = threadIdx.x, j0 = blockIdx.x * 32;
-  const int tok = t >> 3, e0 = t & 7;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int KC = 128, TOK = 8;
+  __shared__ float xs[TOK][KC], ws[N_EXPERT][KC + 1];
+  const int t = threadIdx.x, j0 = blockIdx.x * TOK;
+  const int tok = t >> 5, e = t & 31;
+  float acc = 0.f;
   for (int k0 = 0; k0 < DIM; k0 += KC) {
-    for (int f = t; f < 32 * KC / 4; f += 256) {
+    for (int f = t; f < N_EXPERT * KC / 4; f += 256) {
       const int r = f / (KC / 4), c4 = f % (KC / 4);
-      const int j = min(j0 + r, n - 1);
-      const float4 xv = *(const float4*)(xn + (size_t)j * DIM + k0 + 4 * c4);
       const float4 wv = *(const float4*)(Wr + (size_t)r * DIM + k0 + 4 * c4);
-      xs[r][4 * c4] = xv.x, xs[r][4 * c4 + 1] = xv.y, xs[r][4 * c4 + 2] = xv.z, xs[r][4 * c4 + 3] = xv.w;
       ws[r][4 * c4] = wv.x, ws[r][4 * c4 + 1] = wv.y, ws[r][4 * c4 + 2] = wv.z, ws[r][4 * c4 + 3] = wv.w;
+      if (r < TOK) {
+        const int j = min(j0 + r, n - 1);
+        *(float4*)&xs[r][4 * c4] = *(const float4*)(xn + (size_t)j * DIM + k0 + 4 * c4);
+      }
     }
     __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < KC; k++) {
-      const float xv = xs[tok][k];
-#pragma unroll
-      for (int i = 0; i < 4; i++) acc[i] = fmaf(ws[e0 + 8 * i][k], xv, acc[i]);
-    }
+#pragma unroll 16
+    for (int k = 0; k < KC; k++) acc = fmaf(ws[e][k], xs[tok][k], acc);
     __syncthreads();
   }
-  if (j0 + tok < n)
-#pragma unroll
-    for (int i = 0; i < 4; i++) logits[(size_t)(j0 + tok) * N_EXPERT + e0 + 8 * i] = acc[i];
+  if (j0 + tok < n) logits[(size_t)(j0 + tok) * N_EXPERT + e] = acc;
 }
 
 // Stable per-expert slot lists (kernels/persistent.rs:58-76): block e scans
@@ -419,17 +596,43 @@ void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, fl
 
 void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int start, int n,
                int ctx, float eps, __half* kc, __half* vc, cudaStream_t s) {
-  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, start, ctx, eps, kc, vc);
+  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, start, ctx, eps, kc, vc, nullptr, nullptr, 0);
 }
 
 void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int start, int n, int ctx, float* out,
                   cudaStream_t s) {
-  k_attn_prefill<<<(n * HEADS + 7) / 8, 256, 0, s>>>(qkv, kc, vc, start, n, ctx, out);
+  k_attn_prefill<<<(n * HEADS + 7) / 8, 256, 0, s>>>(qkv, kc, vc, start, n, ctx, out, nullptr, nullptr, 0);
+}
+
+void qk_prep_batch(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int n, int ctx,
+                   float eps, __half* kc, __half* vc, const int* tpos, const int* tsess, size_t sstride,
+                   cudaStream_t s) {
+  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, 0, ctx, eps, kc, vc, tpos, tsess, sstride);
+}
+
+size_t attn_batch_part_floats(int n, int ctx) {
+  return (size_t)n * KV_HEADS * ((ctx + ABS - 1) / ABS) * 4 * (HEAD_DIM + 2);
+}
+
+void attn_batch(const float* qkv, const __half* kc, const __half* vc, int n, int ctx, float* out, const int* tpos,
+                const int* tsess, size_t sstride, float* part, cudaStream_t s) {
+  const int nsplit = (ctx + ABS - 1) / ABS;
+  k_attn_batch<<<dim3(KV_HEADS, nsplit, n), 128, 0, s>>>(qkv, kc, vc, ctx, tpos, tsess, sstride, part, nsplit);
+  k_attn_batch_merge<<<n, HEADS * 32, 0, s>>>(part, tpos, nsplit, out);
+}
+
+void conv_batch(const float* bcx, const float* conv_w, float* state, size_t sstride, const int* tsess, int n,
+                float* gated, cudaStream_t s) {
+  k_conv_batch<<<dim3(DIM / 256, n), 256, 0, s>>>(bcx, conv_w, state, sstride, tsess, n, gated);
+}
+
+void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s) {
+  k_argmax_rows<<<n, 1024, 0, s>>>(x, len, out);
 }
 
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
   static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
-  k_router_logits_n<<<(n + 31) / 32, 256, 0, s>>>(Wr, xnorm, n, logits);
+  k_router_logits_n<<<(n + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {

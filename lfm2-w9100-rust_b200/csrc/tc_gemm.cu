@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "dev_common.cuh"
@@ -232,37 +233,60 @@ __global__ void __launch_bounds__(THREADS, 1)
 // into fp16 range; hi and lo of 128 tokens form the 256 B-rows of one N=256
 // MMA, and the epilogue adds the two halves of the accumulator.
 //
-// Roles (10 warps):
-//   warp 0        TMA: the raw Q6_K planes of the 128-row weight tile, half a
-//                 super-block at a time (3-D box over the quant plane; the
-//                 2-D scale box with the first half; two half buffers), and
-//                 64-wide K chunks of the hi/lo activations into a 5-deep
-//                 ring: the activation tiles come from L2/HBM with ~1.3 us
-//                 latency, and the ring keeps that many bytes in flight
-//   warp 1        TMEM allocation (512 columns: two 128 x 256 accumulators)
-//                 and the MMA issue: 4 x (M=128, N=256, K=16) per chunk
+// Roles (10 warps), for a tile of 128 weight rows x TT tokens (TT = 16, 32,
+// 64 or 128; the MMA is M=128, N=2*TT):
+//   warp 0        TMA, two lanes with independent rings: lane 0 streams the
+//                 64-wide K chunks of the hi/lo activations (5 to 16 deep),
+//                 lane 1 the raw Q6_K planes of the weight tile, half a
+//                 super-block at a time (3-D box over the quant plane, the
+//                 2-D scale box with the first half; 2 to 6 buffers)
+//   warp 1        TMEM allocation (2 or 4 super-block accumulators of 2*TT
+//                 columns) and the MMA issue: 4 x (M=128, N=2*TT, K=16) per
+//                 chunk
 //   warps 2-9     workers, two per tile row: each reads its row's raw
 //                 pieces once per half super-block into registers and writes
-//                 half of every chunk's fp16 sc*(q-32) values into a 2-deep
-//                 ring of swizzled K-major A chunks; one chunk into the next
-//                 super-block it folds the finished accumulator into its 64
-//                 running sums, y += d * (hi + lo); at the end it stores them
+//                 half of every chunk's fp16 sc*(q-32) values into a ring of
+//                 swizzled K-major A chunks; one chunk into a super-block it
+//                 folds an earlier super-block's finished accumulator into
+//                 its TT/2 running sums, y += d * (hi + lo), and at the end
+//                 it stores them
+// The ring depths (activation, A, raw) and the number of accumulators depend
+// on TT: narrow tiles have small activation chunks and little tensor work per
+// chunk, so they keep more chunks of everything in flight.
 // Grouped (routed experts): the activations of each expert are gathered into
 // a contiguous, 128-padded run of hi/lo rows (tc_group, tc_split_grouped), a tile
 // table lists (expert, first row) per token tile, and the epilogue writes
 // each row to its selection slot.
 namespace {
-constexpr int ASTAGES = 2;                    // dequantised A chunks (produced on chip)
-constexpr int BSTAGES = 5;                    // activation chunks (TMA from L2/HBM: the deep ring)
+// Ring depths per token tile: A = dequantised weight chunks (made on chip),
+// B = activation chunks (TMA from L2/HBM, ~1-2 us away: the deep ring), raw =
+// half super-blocks of Q6_K planes. Narrow tiles have small B chunks and run
+// through chunks quickly, so they keep more of everything in flight.
+__host__ __device__ constexpr int q_astages(int tt) { return tt >= 128 ? 2 : (tt >= 64 ? 3 : 4); }
+__host__ __device__ constexpr int q_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 16)); }
 constexpr int QA_BYTES = 128 * 128;           // A chunk: 128 rows x 64 fp16
-constexpr int QB_BYTES = 256 * 128;           // B chunk: 256 rows x 64 fp16
 constexpr int RAWH_Q = 128 * 3 * 32;          // half super-block: 3 pieces x 2 units x 128 rows
 constexpr int RAWH_S = 128 * 16;              // scales of the super-block (with the first half)
 constexpr int RAWH_BYTES = RAWH_Q + RAWH_S;   // 14 KB
-constexpr int OFF_B = ASTAGES * QA_BYTES, OFF_RAW = OFF_B + BSTAGES * QB_BYTES;
+__host__ __device__ constexpr int q_off_b(int tt) { return q_astages(tt) * QA_BYTES; }
+constexpr int RAWN_MAX = 16;
+// Shared memory of the TT-token kernel: A ring, B ring of 2*TT-row chunks, and
+// as many raw half super-block buffers as fit (2 at TT = 128, 12 at TT = 16):
+// narrow tiles stream weights faster than they multiply, so they keep more
+// weight bytes in flight.
+__host__ __device__ constexpr int q_off_raw(int tt) { return q_off_b(tt) + q_bstages(tt) * 2 * tt * 128; }
+__host__ __device__ constexpr int q_rawn(int tt) {
+  return (232448 - 2048 - q_off_raw(tt)) / RAWH_BYTES < RAWN_MAX ? (232448 - 2048 - q_off_raw(tt)) / RAWH_BYTES
+                                                                  : RAWN_MAX;
+}
+__host__ __device__ constexpr int q_smem(int tt) { return q_off_raw(tt) + q_rawn(tt) * RAWH_BYTES + 1024; }
 constexpr int QTHREADS = 10 * 32;
-constexpr int QSMEM = OFF_RAW + 2 * RAWH_BYTES + 1024;
-constexpr uint32_t QTMEM_COLS = 512;
+// Super-block accumulators in TMEM (2 * TT columns each): two at TT = 128
+// (all 512 columns), four for narrower tiles, which lets the workers fold a
+// super-block three super-blocks after it was issued instead of waiting for
+// the tensor core.
+__host__ __device__ constexpr int q_nacc(int tt) { return tt >= 128 ? 2 : 4; }
+__host__ __device__ constexpr uint32_t q_tmem_cols(int tt) { return (uint32_t)(q_nacc(tt) * 2 * tt); }
 
 struct TcQ6Params {
   Q6Mat W;
@@ -276,6 +300,8 @@ struct TcQ6Params {
   const int* tiles;    // grouped: [0] = count, then (expert, first row) pairs
   const int* slots;    // grouped: operand row -> output slot (-1: padding)
   int grouped;
+  int ksplit;          // dense, one token tile: super-blocks split over blockIdx.z
+  float* part;         // ... partial sums [ksplit][ntok][W.rows], reduced by k_tc_reduce
   unsigned* err;
 };
 
@@ -290,17 +316,32 @@ __device__ __forceinline__ void codes_to_h2(uint32_t code, __half2 sc2, uint32_t
   hi = *(uint32_t*)&hb;
 }
 
+// TT: tokens per tile (16, 32, 64 or 128); the MMA is M=128, N=2*TT.
+template <int TT>
 __global__ void __launch_bounds__(QTHREADS, 1)
     k_tc_q6(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapS,
             const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
+  constexpr int QB_BYTES = 2 * TT * 128;
+  constexpr uint32_t QTMEM_COLS = q_tmem_cols(TT);
+  constexpr uint32_t IDESC_Q = idesc_f16(128, 2 * TT, false);
+  constexpr int TH = TT / 2;  // tokens of one worker thread
+  constexpr int ASTAGES = q_astages(TT), BSTAGES = q_bstages(TT);
+  constexpr int NACC = q_nacc(TT), LAG = NACC - 1;  // a super-block is folded LAG super-blocks later
+  constexpr int OFF_B = q_off_b(TT);
+  constexpr int OFF_RAW = q_off_raw(TT);
+  constexpr int RAWN = q_rawn(TT);
+  static_assert(RAWN >= 2, "raw ring");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* raw = smem + OFF_RAW;
-  __shared__ uint64_t bfull[BSTAGES], bempty[BSTAGES], afull[ASTAGES], aempty[ASTAGES], raw_full[2], raw_empty[2],
-      acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint64_t bfull[BSTAGES], bempty[BSTAGES], afull[ASTAGES], aempty[ASTAGES], raw_full[RAWN],
+      raw_empty[RAWN], acc_full[NACC], acc_empty[NACC], mma_done;
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = p.W.nb;
+  // this CTA's super-blocks [kb0, kb0 + nbl) (all of them unless split over K)
+  const int kb0 = (int)((long long)blockIdx.z * nb / p.ksplit);
+  const int nbl = (int)((long long)(blockIdx.z + 1) * nb / p.ksplit) - kb0;
   const int o0 = blockIdx.x * 128;
   int brow0, wrow0;
   if (p.grouped) {
@@ -309,7 +350,7 @@ __global__ void __launch_bounds__(QTHREADS, 1)
     brow0 = p.tiles[2 + 2 * blockIdx.y];
   } else {
     wrow0 = 0;
-    brow0 = blockIdx.y * 128;
+    brow0 = blockIdx.y * TT;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < BSTAGES; s++) {
@@ -321,8 +362,12 @@ __global__ void __launch_bounds__(QTHREADS, 1)
       mbar_init(&aempty[s], 1);
     }
     for (int r = 0; r < 2; r++) {
+    }
+    for (int r = 0; r < RAWN; r++) {
       mbar_init(&raw_full[r], 1);
       mbar_init(&raw_empty[r], 8);
+    }
+    for (int r = 0; r < NACC; r++) {
       mbar_init(&acc_full[r], 1);
       mbar_init(&acc_empty[r], 8);
     }
@@ -334,60 +379,70 @@ __global__ void __launch_bounds__(QTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const int nchunks = 4 * nb;
+  const int nchunks = 4 * nbl;
 
   if (warp == 0) {
     if (lane == 0) {
       // ----------------------------------------------------------- producer
-      // Chunk j = 4b + c. Before the chunks of each half super-block
-      // (c = 0, 2), the raw pieces of that half go into raw buffer (half & 1).
-      int issued = 0, issued_raw = 0;
+      // lane 0: activation chunks j (5-deep ring)
+      int issued = 0;
       bool ok = true;
       for (int j = 0; j < nchunks && ok; j++) {
-        const int b = j >> 2, c = j & 3;
-        if ((c & 1) == 0) {
-          const int k = j >> 1, rb = k & 1;  // half super-block index
-          if (k >= 2 && !(ok = mbar_wait(&raw_empty[rb], ((k >> 1) - 1) & 1, p.err))) break;
-          uint8_t* rq = raw + rb * RAWH_BYTES;
-          mbar_expect_tx(&raw_full[rb], RAWH_Q + (c == 0 ? RAWH_S : 0));
-          tma_load_3d(rq, &mapQ, 64 * b + 32 * (c >> 1), 0, wrow0 + o0, &raw_full[rb]);
-          if (c == 0) tma_load_2d(rq + RAWH_Q, &mapS, 16 * b, wrow0 + o0, &raw_full[rb]);
-          issued_raw = k + 1;
-        }
         const int s = j % BSTAGES, round = j / BSTAGES;
         if (round > 0 && !(ok = mbar_wait(&bempty[s], (round - 1) & 1, p.err))) break;
         uint8_t* bs = smem + OFF_B + s * QB_BYTES;
         mbar_expect_tx(&bfull[s], QB_BYTES);
-        tma_load_2d(bs, &mapX, 64 * j, brow0, &bfull[s]);
-        tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * j, p.rpad + brow0, &bfull[s]);
+        tma_load_2d(bs, &mapX, 64 * (4 * kb0 + j), brow0, &bfull[s]);
+        tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * (4 * kb0 + j), p.rpad + brow0, &bfull[s]);
         issued = j + 1;
       }
       // every issued copy must land before the CTA may exit
       for (int j = issued > BSTAGES ? issued - BSTAGES : 0; j < issued; j++)
         mbar_wait(&bfull[j % BSTAGES], (j / BSTAGES) & 1, nullptr);
-      for (int k = issued_raw > 2 ? issued_raw - 2 : 0; k < issued_raw; k++)
-        mbar_wait(&raw_full[k & 1], (k >> 1) & 1, nullptr);
+    } else if (lane == 1) {
+      // lane 1: raw weight pieces, half super-block k = 2 * (b - kb0) + h into
+      // buffer k % RAWN (runs ahead of the activations by up to RAWN halves)
+      int issued = 0;
+      bool ok = true;
+      for (int k = 0; k < 2 * nbl && ok; k++) {
+        const int b = kb0 + (k >> 1), h = k & 1, rb = k % RAWN;
+        if (k >= RAWN && !(ok = mbar_wait(&raw_empty[rb], ((k / RAWN) - 1) & 1, p.err))) break;
+        uint8_t* rq = raw + rb * RAWH_BYTES;
+        mbar_expect_tx(&raw_full[rb], RAWH_Q + (h == 0 ? RAWH_S : 0));
+        tma_load_3d(rq, &mapQ, 64 * b + 32 * h, 0, wrow0 + o0, &raw_full[rb]);
+        if (h == 0) tma_load_2d(rq + RAWH_Q, &mapS, 16 * b, wrow0 + o0, &raw_full[rb]);
+        issued = k + 1;
+      }
+      for (int k = issued > RAWN ? issued - RAWN : 0; k < issued; k++)
+        mbar_wait(&raw_full[k % RAWN], (k / RAWN) & 1, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // -------------------------------------------------------------- MMA
+      // One thread issues everything, so its per-chunk overhead bounds the
+      // tensor pipe: ring positions and phases advance incrementally and the
+      // descriptors are offsets of two precomputed bases (the start address
+      // field counts 16-byte units; shared addresses stay below 2^18).
       bool ok = true;
-      for (int b = 0; b < nb && ok; b++) {
-        const int a = b & 1;
-        if (b >= 2 && !(ok = mbar_wait(&acc_empty[a], ((b >> 1) - 1) & 1, p.err))) break;
+      int sb = 0, sa = 0;
+      uint32_t pb = 0, pa = 0;
+      const uint64_t dA0 = smem_desc_sw128(smem_u32(smem)), dB0 = smem_desc_sw128(smem_u32(smem + OFF_B));
+      for (int b = 0; b < nbl && ok; b++) {
+        const int a = b % NACC;
+        if (b >= NACC && !(ok = mbar_wait(&acc_empty[a], ((b / NACC) - 1) & 1, p.err))) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(a * 256);
+        const uint32_t d = tmem + (uint32_t)(a * 2 * TT);
         for (int c = 0; c < 4 && ok; c++) {
-          const int j = 4 * b + c, sb = j % BSTAGES, sa = j % ASTAGES;
-          ok = mbar_wait(&bfull[sb], (j / BSTAGES) & 1, p.err) && mbar_wait(&afull[sa], (j / ASTAGES) & 1, p.err);
+          ok = mbar_wait(&bfull[sb], pb, p.err) && mbar_wait(&afull[sa], pa, p.err);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t ua = smem_u32(smem + sa * QA_BYTES), ub = smem_u32(smem + OFF_B + sb * QB_BYTES);
+          const uint64_t da = dA0 + (uint64_t)((sa * QA_BYTES) >> 4), db = dB0 + (uint64_t)((sb * QB_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_f16(d, smem_desc_sw128(ua + kk * 32), smem_desc_sw128(ub + kk * 32), IDESC, (c | kk) ? 1u : 0u);
+          for (int kk = 0; kk < 4; kk++) mma_f16(d, da + 2 * kk, db + 2 * kk, IDESC_Q, (c | kk) ? 1u : 0u);
           mma_commit(&bempty[sb]);
           mma_commit(&aempty[sa]);
+          if (++sb == BSTAGES) sb = 0, pb ^= 1u;
+          if (++sa == ASTAGES) sa = 0, pa ^= 1u;
         }
         mma_commit(&acc_full[a]);
       }
@@ -404,37 +459,48 @@ __global__ void __launch_bounds__(QTHREADS, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const size_t wrow = (size_t)wrow0 + o0 + row;
-    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(64 * g);
-    float y[64];
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(TH * g);
+    float y[TH];
 #pragma unroll
-    for (int j = 0; j < 64; j++) y[j] = 0.f;
+    for (int j = 0; j < TH; j++) y[j] = 0.f;
     bool ok = true;
     // y += d_b * (hi + lo) for super-block b's accumulator
     auto epilogue = [&](int b, float d) {
-      const int a = b & 1;
-      ok = ok && mbar_wait(&acc_full[a], (b >> 1) & 1, p.err);
+      const int a = b % NACC;
+      ok = ok && mbar_wait(&acc_full[a], (b / NACC) & 1, p.err);
       tc_fence_after();
-      const uint32_t base = lane_base + (uint32_t)(a * 256);
+      const uint32_t base = lane_base + (uint32_t)(a * 2 * TT);
+      if constexpr (TH >= 16) {
 #pragma unroll
-      for (int h = 0; h < 4; h++) {
-        uint32_t hi[16], lo[16];
-        tmem_ld16_nowait(base + 16 * h, hi);
-        tmem_ld16_nowait(base + 128 + 16 * h, lo);
+        for (int h = 0; h < TH / 16; h++) {
+          uint32_t hi[16], lo[16];
+          tmem_ld16_nowait(base + 16 * h, hi);
+          tmem_ld16_nowait(base + TT + 16 * h, lo);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j++)
+            y[16 * h + j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[16 * h + j]);
+        }
+      } else {
+        uint32_t hi[8], lo[8];
+        tmem_ld8_nowait(base, hi);
+        tmem_ld8_nowait(base + TT, lo);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; j++)
-          y[16 * h + j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[16 * h + j]);
+        for (int j = 0; j < 8; j++) y[j] = fmaf(d, __uint_as_float(hi[j]) + __uint_as_float(lo[j]), y[j]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     };
-    // d of the super-block being folded, and of the one being dequantised
-    // (loaded a super-block ahead of its use)
-    float d_fold = 0.f, d_next = 0.f;
-    for (int b = 0; b < nb && ok; b++) {
-      d_fold = d_next;
-      d_next = __half2float(p.W.d[wrow * nb + b]);
+    // dd[i] = d of super-block b - i (loaded when b starts, used LAG super-blocks later)
+    float dd[NACC];
+#pragma unroll
+    for (int i = 0; i < NACC; i++) dd[i] = 0.f;
+    for (int b = 0; b < nbl && ok; b++) {
+#pragma unroll
+      for (int i = NACC - 1; i > 0; i--) dd[i] = dd[i - 1];
+      dd[0] = __half2float(p.W.d[wrow * nb + kb0 + b]);
       uint4 ql[2], qh[2];
       uint32_t scw[4];
 #pragma unroll
@@ -443,8 +509,8 @@ __global__ void __launch_bounds__(QTHREADS, 1)
         const int h = c >> 1, m = 2 * (c & 1) + g;
         if ((c & 1) == 0) {
           // this half's pieces (low nibbles: piece g; high bits: piece 2) of units 2h, 2h+1
-          const int k = 2 * b + h, rb = k & 1;
-          if (!(ok = mbar_wait(&raw_full[rb], (k >> 1) & 1, p.err))) break;
+          const int k = 2 * b + h, rb = k % RAWN;
+          if (!(ok = mbar_wait(&raw_full[rb], (k / RAWN) & 1, p.err))) break;
           const uint8_t* rq = raw + rb * RAWH_BYTES + row * 96;
 #pragma unroll
           for (int qq = 0; qq < 2; qq++) {
@@ -485,22 +551,27 @@ __global__ void __launch_bounds__(QTHREADS, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&afull[s]);
-          if ((c & 1) == 0) mbar_arrive(&raw_empty[(2 * b + h) & 1]);  // this half is in registers
+          if ((c & 1) == 0) mbar_arrive(&raw_empty[(2 * b + h) % RAWN]);  // this half is in registers
         }
-        // the previous super-block's accumulator is complete by now: fold it in
-        if (c == 1 && b >= 1) epilogue(b - 1, d_fold);
+        // super-block b - LAG's accumulator is complete by now: fold it in
+        if (c == 1 && b >= LAG) epilogue(b - LAG, dd[LAG]);
       }
     }
-    if (ok) epilogue(nb - 1, d_next);
+    // the last LAG super-blocks, in order (dd[i] holds super-block nbl - 1 - i)
+#pragma unroll
+    for (int i = LAG - 1; i >= 0; i--)
+      if (ok && nbl - 1 - i >= 0) epilogue(nbl - 1 - i, dd[i]);
     if (ok) {
       const int o = o0 + row;
 #pragma unroll
-      for (int j = 0; j < 64; j++) {
-        const int br = brow0 + 64 * g + j;
+      for (int j = 0; j < TH; j++) {
+        const int br = brow0 + TH * g + j;
         const float v = y[j] * __ldg(p.inv + br);
         if (p.grouped) {
           const int slot = __ldg(p.slots + br);
           if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v;
+        } else if (p.part) {
+          if (br < p.ntok) p.part[((size_t)blockIdx.z * p.ntok + br) * p.W.rows + o] = v;
         } else if (br < p.ntok) {
           float* dst = p.out + (size_t)br * p.ldo + o;
           if (p.resid) *dst += v;
@@ -638,12 +709,24 @@ __global__ void __launch_bounds__(256) k_tc_split_norm(const float* X, const flo
   if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
 }
 
+// Split-K partials -> output, the splits summed in order (deterministic):
+// out[t * ldo + o] (+)= sum_s part[s][t][o].
+__global__ void k_tc_reduce(const float* part, int ksplit, int n, int rows, float* out, int ldo, int resid) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)n * rows) return;
+  const int t = (int)(i / rows), o = (int)(i % rows);
+  float v = part[i];
+  for (int s = 1; s < ksplit; s++) v += part[(size_t)s * n * rows + i];
+  float* dst = out + (size_t)t * ldo + o;
+  *dst = resid ? *dst + v : v;
+}
+
 // Grouped layout from the expert lists (groups[e * (cap + 1)] = count, then
 // the selection slots): experts' rows start at 128-aligned bases; tiles =
 // {count, (expert, first row) ...}; slots[row] = selection slot or -1;
 // rowof[slot] = operand row. One block of 1024 threads.
 __global__ void k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots, int* rowof, int nslots,
-                                 int rpad) {
+                                 int rpad, int tt) {
   __shared__ int base[N_EXPERT], cnt[N_EXPERT];
   const int t = threadIdx.x;
   if (t < N_EXPERT) cnt[t] = groups[(size_t)t * (cap + 1)];
@@ -652,13 +735,13 @@ __global__ void k_tc_group_tiles(const int* groups, int cap, int* tiles, int* sl
     int b = 0, nt = 0;
     for (int e = 0; e < N_EXPERT; e++) {
       base[e] = b;
-      const int tiles_e = (cnt[e] + 127) / 128;
+      const int tiles_e = (cnt[e] + tt - 1) / tt;
       for (int i = 0; i < tiles_e; i++) {
         tiles[1 + 2 * nt] = e;
-        tiles[2 + 2 * nt] = b + 128 * i;
+        tiles[2 + 2 * nt] = b + tt * i;
         nt++;
       }
-      b += 128 * tiles_e;
+      b += tt * tiles_e;
     }
     tiles[0] = nt;
   }
@@ -773,24 +856,46 @@ cudaError_t map_raw(CUtensorMap* mq, CUtensorMap* ms, const Q6Mat& W) {
   return cudaSuccess;
 }
 
-int dense_rpad(int n) { return (n + 127) / 128 * 128; }
+// Token tile of a GEMM over n tokens: the smallest of 16/32/64/128 that holds
+// them (dense) or the average expert's share of them (grouped); every
+// activation row a tile loads is streamed once per 128 weight rows, so small
+// batches use narrow tiles.
+int tile_tokens(int per_tile) { return per_tile <= 16 ? 16 : (per_tile <= 32 ? 32 : (per_tile <= 64 ? 64 : 128)); }
+int dense_tt(int n) { return tile_tokens(n); }
+int grouped_tt(int n) { return tile_tokens((n * N_USED + N_EXPERT - 1) / N_EXPERT); }
+int dense_rpad(int n) { const int tt = dense_tt(n); return (n + tt - 1) / tt * tt; }
 int grouped_rpad(int n) { return (int)tc_scratch_rows(n); }
 
 bool fits(const TcScratch& sc, int rpad, int K) {
   return sc.xg && (size_t)rpad <= sc.rows && 2 * (size_t)rpad * (size_t)K <= sc.halves;
 }
 
-cudaError_t launch_q6(const Q6Mat& W, int rpad, int ntiles_y, const TcQ6Params& p, const TcScratch& sc,
+template <int TT>
+cudaError_t launch_q6_tt(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mx, dim3 grid,
+                         const TcQ6Params& p, cudaStream_t s) {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(k_tc_q6<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, q_smem(TT));
+  });
+  k_tc_q6<TT><<<grid, QTHREADS, q_smem(TT), s>>>(mq, ms, mx, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q6(const Q6Mat& W, int rpad, int tt, int ntiles_y, const TcQ6Params& p, const TcScratch& sc,
                       cudaStream_t s) {
   CUtensorMap mq, ms, mx;
   cudaError_t e = map_raw(&mq, &ms, W);
   if (e != cudaSuccess) return e;
-  e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, 128);
+  e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, tt);
   if (e != cudaSuccess) return e;
-  static std::once_flag once;
-  std::call_once(once, [] { cudaFuncSetAttribute(k_tc_q6, cudaFuncAttributeMaxDynamicSharedMemorySize, QSMEM); });
-  k_tc_q6<<<dim3(p.out_rows / 128, ntiles_y), QTHREADS, QSMEM, s>>>(mq, ms, mx, p);
-  return cudaGetLastError();
+  const dim3 grid(p.out_rows / 128, ntiles_y, p.ksplit);
+  switch (tt) {
+    case 16: return launch_q6_tt<16>(mq, ms, mx, grid, p, s);
+    case 32: return launch_q6_tt<32>(mq, ms, mx, grid, p, s);
+    case 64: return launch_q6_tt<64>(mq, ms, mx, grid, p, s);
+    case 128: return launch_q6_tt<128>(mq, ms, mx, grid, p, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 }  // namespace
 
@@ -829,13 +934,31 @@ cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, c
   p.resid = resid ? 1 : 0;
   p.ntok = n;
   p.err = sc.err;
-  return launch_q6(W, rpad, rpad / 128, p, sc, s);
+  p.ksplit = 1;
+  // A single token tile leaves most SMs idle on the narrow matrices: split the
+  // super-blocks over up to ~2 CTAs per SM and reduce the partials in order.
+  const int tt = dense_tt(n);
+  const int ctas = (W.rows / 128) * (rpad / tt);
+  if (rpad == tt && sc.part && ctas < 148) {
+    int ks = std::min(std::min(W.nb, 16), (296 + ctas - 1) / ctas);
+    while (ks > 1 && (size_t)ks * n * W.rows > sc.part_cap) ks--;
+    if (ks > 1) {
+      p.ksplit = ks;
+      p.part = sc.part;
+      cudaError_t e = launch_q6(W, rpad, tt, 1, p, sc, s);
+      if (e != cudaSuccess) return e;
+      const size_t cnt = (size_t)n * W.rows;
+      k_tc_reduce<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(sc.part, ks, n, W.rows, out, ldo, resid ? 1 : 0);
+      return cudaGetLastError();
+    }
+  }
+  return launch_q6(W, rpad, tt, rpad / tt, p, sc, s);
 }
 
 cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s) {
   const int rpad = grouped_rpad(n);
   if (n <= 0 || (size_t)rpad > sc.rows || !sc.tiles || !sc.slots || !sc.rowof) return cudaErrorInvalidValue;
-  k_tc_group_tiles<<<1, 1024, 0, s>>>(groups, cap, sc.tiles, sc.slots, sc.rowof, n * N_USED, rpad);
+  k_tc_group_tiles<<<1, 1024, 0, s>>>(groups, cap, sc.tiles, sc.slots, sc.rowof, n * N_USED, rpad, grouped_tt(n));
   return cudaGetLastError();
 }
 
@@ -863,9 +986,15 @@ cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, 
   p.slots = sc.slots;
   p.grouped = 1;
   p.err = sc.err;
-  return launch_q6(W, rpad, tc_max_tiles(n), p, sc, s);
+  p.ksplit = 1;
+  return launch_q6(W, rpad, grouped_tt(n), tc_max_tiles(n), p, sc, s);
 }
 
-int tc_max_tiles(int n) { return (n * N_USED + 127) / 128 + N_EXPERT; }
+int tc_max_tiles(int n) {
+  const int tt = grouped_tt(n);
+  return (n * N_USED + tt - 1) / tt + N_EXPERT;
+}
+
+int tc_max_tiles_cap(int n) { return std::max(2 * N_EXPERT, (n * N_USED + 127) / 128 + N_EXPERT); }
 
 }  // namespace lfm

@@ -33,18 +33,22 @@ cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, cons
 struct TcScratch {
   __half* xg = nullptr;  // hi rows [0, rpad) then lo rows [rpad, 2 rpad), K halves each
   float* inv = nullptr;  // [rows]
-  int* tiles = nullptr;  // [1 + 2 * tc_max_tiles(n)]
+  int* tiles = nullptr;  // [1 + 2 * tc_max_tiles_cap(n)]
   int* slots = nullptr;  // [rows]
   int* rowof = nullptr;  // [n * N_USED]
   unsigned* err = nullptr;
+  float* part = nullptr; // split-K partial sums of single-tile GEMMs (optional)
+  size_t part_cap = 0;   // floats
   size_t rows = 0;       // operand rows (tc_scratch_rows of the largest n)
   size_t halves = 0;     // capacity of xg
 };
 // Operand rows needed for n tokens in the grouped case (n * 4 selection slots
 // plus 128-row padding per expert); the dense case needs n rounded up to 128.
 size_t tc_scratch_rows(int n);
-// Most token tiles a grouped GEMM of n tokens can have.
+// Most token tiles a grouped GEMM of n tokens can have, and the most of any
+// GEMM of at most n tokens (the tile table's capacity).
 int tc_max_tiles(int n);
+int tc_max_tiles_cap(int n);
 // The tensor-core path serves this matrix: 128-row output tiles.
 bool tc_q6_supported(const Q6Mat& W, int out_rows);
 

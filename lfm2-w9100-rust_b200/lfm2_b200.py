@@ -45,6 +45,7 @@ _lib = None
 EXPORTS = [
     "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
     "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
+    "lfm_batch_create", "lfm_batch_prefill", "lfm_batch_decode", "lfm_batch_logits",
     "lfm_step_trace", "lfm_engine_info",
     "lfm_reset_session",
     "lfm_snapshot_cache", "lfm_restore_cache", "lfm_snapshot_logits", "lfm_counters_get",
@@ -75,6 +76,10 @@ def lib() -> ctypes.CDLL:
         "lfm_generate": ([P, P, U32, U32, U32, P, ctypes.POINTER(U32)], st),
         "lfm_decode_loop": ([P, U32, U32, U32, P, ctypes.POINTER(ctypes.c_float)], st),
         "lfm_last_device_ms": ([P], ctypes.c_float),
+        "lfm_batch_create": ([P, U32], st),
+        "lfm_batch_prefill": ([P, U32, P, U32, ctypes.POINTER(U32)], st),
+        "lfm_batch_decode": ([P, P, P, P, U32, P], st),
+        "lfm_batch_logits": ([P, U32, P], st),
         "lfm_step_trace": ([P, ctypes.c_int, P, SZ, ctypes.POINTER(U32), ctypes.POINTER(U32)], st),
         "lfm_engine_info": ([P], ctypes.c_char_p),
         "lfm_reset_session": ([P], st),
@@ -185,6 +190,31 @@ class GpuEngine:
 
     def last_device_ms(self) -> float:
         return float(lib().lfm_last_device_ms(self.h))
+
+    # -------- independent sessions decoded together (lfm_batch_*)
+    def batch_create(self, n_sessions: int):
+        self._check(lib().lfm_batch_create(self.h, n_sessions), "batch_create")
+
+    def batch_prefill(self, session: int, ids) -> int:
+        """Fresh prompt of one session; returns its greedy next token."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        t = ctypes.c_uint32()
+        self._check(lib().lfm_batch_prefill(self.h, session, _p(ids), len(ids), ctypes.byref(t)), "batch_prefill")
+        return int(t.value)
+
+    def batch_decode(self, sessions, tokens, positions) -> np.ndarray:
+        """One decode step of distinct sessions; returns their next tokens."""
+        ss = np.ascontiguousarray(sessions, dtype=np.uint32)
+        tt = np.ascontiguousarray(tokens, dtype=np.uint32)
+        pp = np.ascontiguousarray(positions, dtype=np.uint32)
+        out = np.empty(len(ss), dtype=np.uint32)
+        self._check(lib().lfm_batch_decode(self.h, _p(ss), _p(tt), _p(pp), len(ss), _p(out)), "batch_decode")
+        return out
+
+    def batch_logits(self, index: int) -> np.ndarray:
+        out = np.empty(self.vocab, dtype=np.float32)
+        self._check(lib().lfm_batch_logits(self.h, index, _p(out)), "batch_logits")
+        return out
 
     def step_trace(self, enable: bool):
         """Switch per-stage timestamps of the persistent decode step on/off and
