@@ -281,6 +281,14 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
                                   const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_div,
                                   uint32_t n, float* y_dev, void* stream);
 
+/* Failure-detection self-test (no counterpart in the reference, whose
+ * watchdog handling is vulkan/fence_stop.rs): one thread waits on an
+ * mbarrier that nothing completes, through the library's bounded wait (about
+ * one second of SM cycles). On return *status holds the device status word
+ * the wait raised (1 = timed out; 0 or 99 would mean the bound failed) and
+ * *cycles the SM cycles the wait took. Synchronous; the context stays usable. */
+lfm_status lfm_selftest_wait_timeout(uint32_t* status, uint64_t* cycles);
+
 /* Message of the last failing kernel-level call on this thread. */
 const char* lfm_ops_error(void);
 

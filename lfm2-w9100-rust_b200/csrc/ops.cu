@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "../../include/lfm_cuda.h"
+#include "dev_common.cuh"
 #include "kernels.h"
 #include "tc_gemm.h"
 
@@ -26,6 +27,23 @@ bool shape_ok(uint32_t in_dim, uint32_t rows) { return in_dim >= 256 && in_dim %
 
 // status word of lfm_tc_gemm_f16 (raised by a bounded wait that timed out)
 __device__ unsigned g_tc_err;
+
+// Failure-detection self-test: thread 0 waits on an mbarrier that nothing
+// arrives at, through the same bounded wait every kernel of the library uses
+// (lfm::dev::mbar_wait, about one second of SM cycles). It must give up,
+// raise the status word and return; the kernel then exits normally and the
+// context stays usable. No fault, trap or unbounded spin is involved.
+__global__ void k_selftest_wait_timeout(unsigned* err, unsigned long long* cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    lfm::dev::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const long long t0 = clock64();
+    const bool ok = lfm::dev::mbar_wait(&bar, 0, err);  // phase 0 never completes
+    *cycles = (unsigned long long)(clock64() - t0);
+    if (ok) atomicExch(err, 99u);  // a wait that returned success would be a bug
+  }
+}
 }  // namespace
 
 extern "C" {
@@ -240,6 +258,32 @@ lfm_status lfm_attention_prefill(const float* q_dev, uint32_t q_stride, const vo
     e = lfm::attn_prefill_tc(q_dev, (int)q_stride, (const __half*)k_cache, (const __half*)v_cache, (int)start,
                              (int)n, (int)ctx, out_dev, (int)out_stride, cs.sc.err, s);
   return cs.finish(e, "lfm_attention_prefill");
+}
+
+lfm_status lfm_selftest_wait_timeout(uint32_t* status, uint64_t* cycles) {
+  if (!status || !cycles) {
+    t_err = "lfm_selftest_wait_timeout: bad argument";
+    return LFM_ERR_ARG;
+  }
+  unsigned* err = nullptr;
+  unsigned long long* cyc = nullptr;
+  cudaError_t e = cudaGetSymbolAddress((void**)&err, g_tc_err);
+  if (e == cudaSuccess) e = cudaMemset(err, 0, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&cyc, sizeof(unsigned long long));
+  if (e == cudaSuccess) {
+    k_selftest_wait_timeout<<<1, 32>>>(err, cyc);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  unsigned h = 0;
+  unsigned long long hc = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h, err, sizeof h, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(&hc, cyc, sizeof hc, cudaMemcpyDeviceToHost);
+  if (cyc) cudaFree(cyc);
+  if (e != cudaSuccess) return cuda_status(e);
+  *status = h;
+  *cycles = hc;
+  return LFM_OK;
 }
 
 lfm_status lfm_tc_gemm_f16_bmn(const void* a_dev, const void* b_dev, uint32_t m, uint32_t k, float* c_dev,

@@ -51,7 +51,7 @@ EXPORTS = [
     "lfm_snapshot_cache", "lfm_restore_cache", "lfm_snapshot_logits", "lfm_counters_get",
     "lfm_device_name", "lfm_last_error", "lfm_global_error", "lfm_q6k_device_bytes",
     "lfm_q6k_upload", "lfm_q6k_dequant", "lfm_q6k_matmul", "lfm_q6k_routed", "lfm_route",
-    "lfm_argmax", "lfm_argmax_noalloc", "lfm_tc_gemm_f16", "lfm_tc_gemm_f16_bmn", "lfm_attention_prefill", "lfm_q6k_prompt_gemm", "lfm_q6k_prompt_grouped",
+    "lfm_argmax", "lfm_argmax_noalloc", "lfm_tc_gemm_f16", "lfm_tc_gemm_f16_bmn", "lfm_attention_prefill", "lfm_selftest_wait_timeout", "lfm_q6k_prompt_gemm", "lfm_q6k_prompt_grouped",
     "lfm_ops_error",
 ]
 
@@ -101,6 +101,7 @@ def lib() -> ctypes.CDLL:
         "lfm_tc_gemm_f16": ([P, P, U32, U32, U32, P, P], st),
         "lfm_tc_gemm_f16_bmn": ([P, P, U32, U32, P, P], st),
         "lfm_attention_prefill": ([P, U32, P, P, U32, U32, U32, P, U32, P], st),
+        "lfm_selftest_wait_timeout": ([ctypes.POINTER(U32), ctypes.POINTER(ctypes.c_uint64)], st),
         "lfm_q6k_prompt_gemm": ([P, U32, U32, P, U32, P, P], st),
         "lfm_q6k_prompt_grouped": ([P, U32, U32, U32, P, P, U32, U32, P, P], st),
         "lfm_ops_error": ([], ctypes.c_char_p),
