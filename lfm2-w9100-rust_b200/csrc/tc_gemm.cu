@@ -262,8 +262,12 @@ namespace {
 // B = activation chunks (TMA from L2/HBM, ~1-2 us away: the deep ring), raw =
 // half super-blocks of Q6_K planes. Narrow tiles have small B chunks and run
 // through chunks quickly, so they keep more of everything in flight.
-__host__ __device__ constexpr int q_astages(int tt) { return tt >= 128 ? 2 : (tt >= 64 ? 3 : 4); }
-__host__ __device__ constexpr int q_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 16)); }
+// The 16-token tile (routed experts of small batches) is bound by the latency
+// of its per-chunk hand-offs, not by any pipe, so it is sized for two CTAs
+// per SM (~106 KB of shared memory each) to overlap two such chains.
+__host__ __device__ constexpr int q_ctas_per_sm(int tt) { return tt <= 16 ? 2 : 1; }
+__host__ __device__ constexpr int q_astages(int tt) { return tt >= 128 ? 2 : (tt >= 64 ? 3 : (tt >= 32 ? 4 : 2)); }
+__host__ __device__ constexpr int q_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 8)); }
 constexpr int QA_BYTES = 128 * 128;           // A chunk: 128 rows x 64 fp16
 constexpr int RAWH_Q = 128 * 3 * 32;          // half super-block: 3 pieces x 2 units x 128 rows
 constexpr int RAWH_S = 128 * 16;              // scales of the super-block (with the first half)
@@ -275,9 +279,10 @@ constexpr int RAWN_MAX = 16;
 // narrow tiles stream weights faster than they multiply, so they keep more
 // weight bytes in flight.
 __host__ __device__ constexpr int q_off_raw(int tt) { return q_off_b(tt) + q_bstages(tt) * 2 * tt * 128; }
+__host__ __device__ constexpr int q_smem_budget(int tt) { return q_ctas_per_sm(tt) == 2 ? 110 * 1024 : 232448 - 2048; }
 __host__ __device__ constexpr int q_rawn(int tt) {
-  return (232448 - 2048 - q_off_raw(tt)) / RAWH_BYTES < RAWN_MAX ? (232448 - 2048 - q_off_raw(tt)) / RAWH_BYTES
-                                                                  : RAWN_MAX;
+  return (q_smem_budget(tt) - q_off_raw(tt)) / RAWH_BYTES < RAWN_MAX ? (q_smem_budget(tt) - q_off_raw(tt)) / RAWH_BYTES
+                                                                      : RAWN_MAX;
 }
 __host__ __device__ constexpr int q_smem(int tt) { return q_off_raw(tt) + q_rawn(tt) * RAWH_BYTES + 1024; }
 constexpr int QTHREADS = 10 * 32;
@@ -318,7 +323,7 @@ __device__ __forceinline__ void codes_to_h2(uint32_t code, __half2 sc2, uint32_t
 
 // TT: tokens per tile (16, 32, 64 or 128); the MMA is M=128, N=2*TT.
 template <int TT>
-__global__ void __launch_bounds__(QTHREADS, 1)
+__global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
     k_tc_q6(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapS,
             const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
   constexpr int QB_BYTES = 2 * TT * 128;
