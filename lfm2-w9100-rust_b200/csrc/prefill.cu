@@ -499,6 +499,32 @@ __global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const 
   if (j0 + tok < n) logits[(size_t)(j0 + tok) * N_EXPERT + e] = acc;
 }
 
+// Router logits for few tokens (batched decode): one block per token, x
+// staged in shared memory, warp w computes experts w, w+8, w+16, w+24 with
+// lane-strided K and a warp reduction.
+__global__ void __launch_bounds__(256) k_router_logits_tok(const float* Wr, const float* xn, float* logits) {
+  __shared__ float4 xs[DIM / 4];
+  const int j = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float4* x = (const float4*)(xn + (size_t)j * DIM);
+  for (int i = threadIdx.x; i < DIM / 4; i += 256) xs[i] = x[i];
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < N_EXPERT / 8; q++) {
+    const int e = warp + 8 * q;
+    const float4* w = (const float4*)(Wr + (size_t)e * DIM);
+    float a = 0.f;
+    for (int i = lane; i < DIM / 4; i += 32) {
+      const float4 v = w[i], xv = xs[i];
+      a = fmaf(v.x, xv.x, a);
+      a = fmaf(v.y, xv.y, a);
+      a = fmaf(v.z, xv.z, a);
+      a = fmaf(v.w, xv.w, a);
+    }
+    a = warp_sum(a);
+    if (lane == 0) logits[(size_t)j * N_EXPERT + e] = a;
+  }
+}
+
 // Stable per-expert slot lists (kernels/persistent.rs:58-76): block e scans
 // the slots (token*4 + rank) in order, 1024 at a time, and appends those
 // routed to e (ballot within warps, prefix over the block's warps).
@@ -632,7 +658,8 @@ void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s) {
 
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
   static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
-  k_router_logits_n<<<(n + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
+  if (n < 256) k_router_logits_tok<<<n, 256, 0, s>>>(Wr, xnorm, logits);  // few tokens: a block each
+  else k_router_logits_n<<<(n + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {

@@ -266,8 +266,8 @@ namespace {
 // of its per-chunk hand-offs, not by any pipe, so it is sized for two CTAs
 // per SM (~106 KB of shared memory each) to overlap two such chains.
 __host__ __device__ constexpr int q_ctas_per_sm(int tt) { return tt <= 16 ? 2 : 1; }
-__host__ __device__ constexpr int q_astages(int tt) { return tt >= 128 ? 2 : (tt >= 64 ? 3 : (tt >= 32 ? 4 : 2)); }
-__host__ __device__ constexpr int q_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 8)); }
+__host__ __device__ constexpr int q_astages(int tt) { return tt >= 128 ? 2 : (tt >= 64 ? 3 : (tt >= 32 ? 4 : 3)); }
+__host__ __device__ constexpr int q_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 6)); }
 constexpr int QA_BYTES = 128 * 128;           // A chunk: 128 rows x 64 fp16
 constexpr int RAWH_Q = 128 * 3 * 32;          // half super-block: 3 pieces x 2 units x 128 rows
 constexpr int RAWH_S = 128 * 16;              // scales of the super-block (with the first half)
