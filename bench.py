@@ -360,6 +360,7 @@ def main():
     ap.add_argument("--no-micro", action="store_true")
     ap.add_argument("--micro-only", action="store_true", help="only the config-1 Q6_K matvec microbench")
     ap.add_argument("--no-sessions", action="store_true", help="skip config 4 (64 independent sessions per GPU)")
+    ap.add_argument("--sessions-only", action="store_true", help="only config 4 on this GPU (profiling entry point)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
                     help="only one warm-up and one timed N-token prefill (profiling entry point)")
     args = ap.parse_args()
@@ -372,6 +373,17 @@ def main():
     if args.prefill_only:
         if rank == 0:
             print(json.dumps(prefill_only(local, args.prefill_only)), flush=True)
+        return
+    if args.sessions_only:
+        if rank == 0:
+            import torch
+
+            import lfm2_b200
+            torch.cuda.set_device(local)
+            eng = lfm2_b200.GpuEngine(model_path(0, None), local)
+            eng.set_ctx(4096)
+            print(json.dumps(multi_session(eng, measured_peaks(), None, 1, eng.info())), flush=True)
+            eng.close()
         return
     if args.impl == "reference":
         run_reference(args, ws, rank, pg)
