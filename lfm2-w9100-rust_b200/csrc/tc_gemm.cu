@@ -727,39 +727,55 @@ __global__ void k_tc_reduce(const float* part, int ksplit, int n, int rows, floa
 }
 
 // Grouped layout from the expert lists (groups[e * (cap + 1)] = count, then
-// the selection slots): experts' rows start at 128-aligned bases; tiles =
+// the selection slots): experts' rows start at tt-aligned bases; tiles =
 // {count, (expert, first row) ...}; slots[row] = selection slot or -1;
-// rowof[slot] = operand row. One block of 1024 threads.
-__global__ void k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots, int* rowof, int nslots,
-                                 int rpad, int tt) {
-  __shared__ int base[N_EXPERT], cnt[N_EXPERT];
-  const int t = threadIdx.x;
-  if (t < N_EXPERT) cnt[t] = groups[(size_t)t * (cap + 1)];
-  __syncthreads();
-  if (t == 0) {
-    int b = 0, nt = 0;
-    for (int e = 0; e < N_EXPERT; e++) {
-      base[e] = b;
-      const int tiles_e = (cnt[e] + tt - 1) / tt;
-      for (int i = 0; i < tiles_e; i++) {
-        tiles[1 + 2 * nt] = e;
-        tiles[2 + 2 * nt] = b + tt * i;
-        nt++;
-      }
-      b += tt * tiles_e;
+// rowof[slot] = operand row. One block of 1024 threads: warp 0 scans the
+// counts, then every (expert, entry) pair is placed in one flat pass.
+__global__ void __launch_bounds__(1024) k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots,
+                                                         int* rowof, int nslots, int rpad, int tt) {
+  __shared__ int base[N_EXPERT + 1], first[N_EXPERT + 1], tile0[N_EXPERT + 1];
+  const int t = threadIdx.x, lane = t & 31;
+  if (t < 32) {
+    const int cnt = lane < N_EXPERT ? groups[(size_t)lane * (cap + 1)] : 0;
+    const int nt = (cnt + tt - 1) / tt;
+    // inclusive scans of the padded rows, the entries and the tiles
+    int rows = nt * tt, ent = cnt, til = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int r2 = __shfl_up_sync(0xffffffffu, rows, o), e2 = __shfl_up_sync(0xffffffffu, ent, o),
+                t2 = __shfl_up_sync(0xffffffffu, til, o);
+      if (lane >= o) rows += r2, ent += e2, til += t2;
     }
-    tiles[0] = nt;
+    if (lane < N_EXPERT) {
+      base[lane + 1] = rows;
+      first[lane + 1] = ent;
+      tile0[lane + 1] = til;
+    }
+    if (lane == 0) base[0] = first[0] = tile0[0] = 0;
+  }
+  __syncthreads();
+  const int total = first[N_EXPERT];
+  if (t == 0) tiles[0] = tile0[N_EXPERT];
+  for (int i = t; i < tile0[N_EXPERT]; i += blockDim.x) {
+    int e = 0;
+    while (tile0[e + 1] <= i) e++;
+    tiles[1 + 2 * i] = e;
+    tiles[2 + 2 * i] = base[e] + tt * (i - tile0[e]);
   }
   for (int r = t; r < rpad; r += blockDim.x) slots[r] = -1;
   for (int q = t; q < nslots; q += blockDim.x) rowof[q] = -1;
   __syncthreads();
-  for (int e = 0; e < N_EXPERT; e++) {
-    const int* g = groups + (size_t)e * (cap + 1);
-    for (int i = t; i < cnt[e]; i += blockDim.x) {
-      const int slot = g[1 + i];
-      slots[base[e] + i] = slot;
-      rowof[slot] = base[e] + i;
+  for (int f = t; f < total; f += blockDim.x) {
+    int lo = 0, hi = N_EXPERT - 1;  // expert e with first[e] <= f < first[e + 1]
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (first[mid] <= f) lo = mid;
+      else hi = mid - 1;
     }
+    const int e = lo, i = f - first[e];
+    const int slot = groups[(size_t)e * (cap + 1) + 1 + i];
+    slots[base[e] + i] = slot;
+    rowof[slot] = base[e] + i;
   }
 }
 

@@ -1,0 +1,45 @@
+"""Prompt lengths around the tensor-core GEMM's tile boundaries against the
+CPU oracle.
+
+The prompt path picks a token tile of 16/32/64/128 tokens per GEMM (the
+smallest holding the prompt, or for the routed experts the average expert's
+share), splits single-tile GEMMs over K, and pads the last tile; attention
+walks 128-position key tiles. Lengths just past each boundary exercise the
+padding and the split. Contract as in the full-model tests (lfm.rs forward,
+main.rs:174-195): last-token logits max-abs <= 1e-2 against the oracle, same
+argmax wherever the oracle's top-2 margin exceeds twice the observed error.
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def engine(synth_model, cuda_lib):
+    import lfm2_b200
+    e = lfm2_b200.GpuEngine(synth_model, 0)
+    yield e
+    e.close()
+
+
+@pytest.mark.parametrize("n", [17, 33, 65, 129, 200])
+def test_prefill_logits_vs_oracle(engine, synth_model, oracle_mod, n):
+    p = np.random.default_rng(1000 + n).integers(0, 128000, n).astype(np.uint32)
+    o = oracle_mod.OracleEngine(synth_model, kv_f16=True)
+    try:
+        o.set_ctx(n + 16)
+        ref = o.forward(p, 0)
+    finally:
+        o.close()
+    engine.set_ctx(n + 16)
+    engine.reset_session()
+    got = engine.forward(p, 0)
+    err = float(np.abs(got - ref).max())
+    assert err <= TOL, err
+    top = np.sort(ref)[-2:]
+    if top[1] - top[0] > 2 * err:
+        assert int(np.argmax(got)) == int(np.argmax(ref))
