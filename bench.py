@@ -232,6 +232,7 @@ def cpu_baseline(path: str, steps: int, warmup: int, threads: int | None = None)
     oracle.build()
     if threads:
         os.environ["OMP_NUM_THREADS"] = str(threads)
+        oracle.lib().oracle_set_threads(threads)
     o = oracle.OracleEngine(path, kv_f16=True)
     cores = oracle.lib().oracle_num_threads()
     o.set_ctx(4096)
@@ -262,7 +263,8 @@ def run_reference(args, ws, rank, pg):
     path = model_path(0, None)
     steps = min(args.steps, 32)
     warm = min(args.warmup, 3)
-    cb = cpu_baseline(path, steps, warm)
+    # all the host threads this process may use (torchrun sets OMP_NUM_THREADS=1)
+    cb = cpu_baseline(path, steps, warm, threads=len(os.sched_getaffinity(0)))
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -476,7 +478,7 @@ def main():
     cpu = None
     eng.close()  # release the device before the CPU leg and before interpreter teardown
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = cpu_baseline(path, 16, 2)
+        cpu = cpu_baseline(path, 16, 2, threads=len(os.sched_getaffinity(0)))
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,

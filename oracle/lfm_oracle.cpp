@@ -998,6 +998,17 @@ int oracle_num_threads() {
 #endif
 }
 
+// Thread count of the parallel loops (output rows / experts). Set explicitly
+// because a host process may have initialised the OpenMP runtime with
+// OMP_NUM_THREADS=1 (torchrun does) before this library was loaded.
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 }  // extern "C"
 
 // ===================================================================== CLI

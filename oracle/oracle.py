@@ -66,6 +66,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_greedy.argtypes = [P, P, I32, I32, U32, P, P]
         L.oracle_greedy.restype = I32
         L.oracle_num_threads.restype = I32
+        L.oracle_set_threads.argtypes = [I32]
+        L.oracle_set_threads.restype = None
         _lib = L
     return _lib
 
