@@ -253,7 +253,9 @@ struct ConsShared {
 // warps at the start of the expert gate/up stage; `buf` is scratch shared
 // memory of at least G * 33 floats. The result goes to cs.psel / cs.pselw and
 // the producer is released through cs.route_bar.
-__device__ void route_layer(const StepParams& P, const float* bias, ConsShared& cs, float* buf) {
+// Returns, to every consumer thread, the layer input's sum of squares (the
+// 1/rms of both the router and the FFN input).
+__device__ float route_layer(const StepParams& P, const float* bias, ConsShared& cs, float* buf) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const StepCtl* ctl = P.ctl;
   const int G = gridDim.x;
@@ -302,7 +304,9 @@ __device__ void route_layer(const StepParams& P, const float* bias, ConsShared& 
     __syncwarp();
     if (lane == 0) mbar_arrive(&cs.route_bar);  // release: psel/pselw are written
   }
+  const float ss_all = buf[gridDim.x * (N_EXPERT + 1) + N_EXPERT];
   cons_sync();  // buf is reused by the activation staging
+  return ss_all;
 }
 
 // The producer warp: all ring tiles of this CTA, in stage order (lane 0
@@ -441,9 +445,30 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   const bool live = lane < UL;
   const int u = (TYPE == ST_DOWN28 ? (warp & 3) * 28 : 0) + (live ? lane : lane - UL);
   const int vec = TYPE == ST_XDOWN ? warp >> 2 : 0;
-  if (TYPE == ST_XSWIGLU) route_layer(P, stage_table(ring)[S.dep].bias, cs, xsm);
   float xr[64];
-  stage_x<TYPE>(P, S, cs, xsm, xr, u, vec);
+  if (TYPE == ST_XSWIGLU) {
+    // The FFN input's loads go out before the routing (one L2 round trip for
+    // both), and its RMS factor is the routing's sum of squares (the same
+    // vector), so the staging needs no reduction of its own.
+    const float4 v = __ldcg((const float4*)S.xin + threadIdx.x);
+    const float4 g = __ldg((const float4*)S.norm + threadIdx.x);
+    const float ss = route_layer(P, stage_table(ring)[S.dep].bias, cs, xsm);
+    const float inv = 1.0f / sqrtf(ss / (float)DIM + P.eps);
+    *(float4*)&xsm[xs_index(4 * threadIdx.x, DIM / 64)] =
+        make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+    cons_sync();
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const float4 q = *(const float4*)&xsm[(j * (DIM / 64) + u) * 4];
+      xr[4 * j + 0] = q.x;
+      xr[4 * j + 1] = q.y;
+      xr[4 * j + 2] = q.z;
+      xr[4 * j + 3] = q.w;
+    }
+    cons_sync();
+  } else {
+    stage_x<TYPE>(P, S, cs, xsm, xr, u, vec);
+  }
   const bool tr = P.trace && threadIdx.x == 0;
   if (tr) P.trace[((size_t)sidx * gridDim.x + blockIdx.x) * STEP_TRACE_FIELDS + 1] = gtime();
   // tile rows of this warp (DOWN28: row w/4 of the tile in the smem row order)
