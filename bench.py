@@ -465,10 +465,19 @@ def main():
         eng.forward(p3840, 0)
         pms = reduce_max(pg, eng.last_device_ms())
         fl = prefill_flops(PREFILL_LEN)
+        # config 3 continues with 256 greedy tokens up to the 4096-token limit
+        first = int(np.argmax(eng.snapshot_resident_logits()))
+        n_long = 4096 - PREFILL_LEN - 1
+        _, lms = eng.decode_loop(first, PREFILL_LEN, n_long)
+        lms = reduce_max(pg, lms)
+        long_bpt = decode_bytes_per_token(PREFILL_LEN + n_long / 2.0)["total"]
         prefill = {"prompt_len": PREFILL_LEN, "tok_s": round(ws * PREFILL_LEN / (pms / 1000), 1),
                    "ms": round(pms, 2), "tflops": round(fl / (pms / 1000) / 1e12, 2),
                    "frac_of_bf16_peak": round(fl / (pms / 1000) / 1e12 / peaks["bf16_tflops"], 4),
-                   "path": info.get("prefill_path", "")}
+                   "path": info.get("prefill_path", ""),
+                   "decode_after": {"tokens": n_long, "ctx": f"{PREFILL_LEN}..4095",
+                                    "tok_s": round(ws * (n_long - 1) / (lms / 1000), 1),
+                                    "hbm_frac": round(long_bpt * (n_long - 1) / (lms / 1000) / 1e9 / peaks["hbm_gbs"], 4)}}
     multi = None
     if not args.no_sessions:
         multi = multi_session(eng, peaks, pg, ws, info)

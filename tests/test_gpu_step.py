@@ -125,3 +125,22 @@ def test_step_trace_record(step_engine):
     assert (start[1:].min(axis=1) >= done[:-1].min(axis=1)).all()
     # ring stages report their tile counts; their sum over CTAs is the stage's tile count
     assert tr[-1, :, 5].sum() == 128000 // 16
+
+
+def test_step_long_context_matches_chain(step_engine, synth_model):
+    """Config 3's tail: greedy decode from position 3840 to the 4096-token
+    limit, persistent step vs kernel chain (two independent decode paths over
+    the same prefilled state: identical tokens)."""
+    p = np.random.default_rng(11).integers(0, 128000, 3840).astype(np.uint32)
+    chain = _engine(synth_model, False)
+    try:
+        runs = []
+        for e in (step_engine, chain):
+            e.set_ctx(4096)
+            e.reset_session()
+            first = int(np.argmax(e.forward(p, 0)))
+            toks, _ = e.decode_loop(first, len(p), 4096 - len(p))
+            runs.append([first] + toks)
+        assert runs[0] == runs[1]
+    finally:
+        chain.close()
