@@ -825,11 +825,8 @@ cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, f
   e = tc_map_f16(&mb, B, N, K, TN);
   if (e != cudaSuccess) return e;
   const int smem = STAGES * STAGE_BYTES + 1024;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_tc_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  static std::once_flag once;
+  std::call_once(once, [smem] { cudaFuncSetAttribute(k_tc_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
   k_tc_f16<<<dim3(M / TM, N / TN), THREADS, smem, s>>>(ma, mb, C, M, N, K, err);
   return cudaGetLastError();
 }
