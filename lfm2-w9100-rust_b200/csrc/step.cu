@@ -48,6 +48,11 @@ constexpr int PRODUCER = NCW;          // warp index of the producer
 constexpr int RING = 4;
 constexpr int SLOT = 40320;            // 24 rows x (1536 + 128 + 16): the largest tile
 constexpr int KP = HEAD_DIM + 8;       // padded fp16 K row in shared memory
+// 32-position chunks per attention task: at most 32 tasks per kv head, so a
+// 4096-token context needs 4 (the loop is unrolled to this bound; a loop
+// carrying the group barriers cost the tile loops registers)
+constexpr int ATTN_MAX_CPT = 4;
+static_assert(ATTN_MAX_CPT * 32 * ATTN_SPLIT >= 4096, "context limit needs more chunks per task");
 
 struct AttnSmem {
   float sq[4][HEAD_DIM];
@@ -260,9 +265,21 @@ __device__ float route_layer(const StepParams& P, const float* bias, ConsShared&
   const StepCtl* ctl = P.ctl;
   const int G = gridDim.x;
   constexpr int W = N_EXPERT + 1;
-  // one round of loads: the G x 33 partials into shared memory
+  // one round of loads: the G x 33 partials into shared memory (all of a
+  // thread's loads issued before the first store)
   const float* src = &ctl->rpart[0][0];
-  for (int f = threadIdx.x; f < G * W; f += NCW * 32) buf[f] = __ldcg(src + f);
+  constexpr int RP = (STEP_MAX_CTAS * W + NCW * 32 - 1) / (NCW * 32);
+  float rv[RP];
+#pragma unroll
+  for (int i = 0; i < RP; i++) {
+    const int f = threadIdx.x + i * NCW * 32;
+    rv[i] = f < G * W ? __ldcg(src + f) : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < RP; i++) {
+    const int f = threadIdx.x + i * NCW * 32;
+    if (f < G * W) buf[f] = rv[i];
+  }
   cons_sync();
   // column sums in a fixed order: lane l adds CTAs l, l+32, ... then a fixed
   // butterfly across the warp; warp w handles columns w, w+16, w+32
@@ -627,12 +644,21 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   return true;
 }
 
-// Attention task (kv head kh, split) for a 4-warp group g (head = warp & 3).
-__device__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm, int g, int kh, int split, int pos,
-                          int nact) {
+// Attention task (kv head kh, task j of ntask) for a 4-warp group g (head =
+// warp & 3): chunks [c0, c1) of 32 positions with an online softmax, the next
+// chunk's K/V rows loaded into registers while this one is computed. The
+// partial (unnormalised o, running max m, sum l) goes to attn_part; the last
+// task of the kv head to finish merges the head's ntask partials (lane-parallel
+// statistics, batched loads). Same math as engine/src/lfm.rs:396-433 (scores
+// * 1/sqrt(64), softmax over positions 0..=pos, weighted V) with fp32 sums in
+// chunk order instead of f64 sums in position order.
+__device__ __noinline__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm, int g, int kh, int j,
+                                       int ntask, int cpt, int pos) {
   const int w4 = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31, gt = threadIdx.x & 127;
   constexpr int SPL = ATTN_SPLIT;
-  const int t0 = split * SPL;
+  constexpr int PSTR = 4 * (HEAD_DIM + 2);  // floats between one head's partials of consecutive tasks
+  const int nchunk = pos / SPL + 1;
+  const int c0 = j * cpt, c1 = min(c0 + cpt, nchunk);
   const int nsplit = (P.ctx + SPL - 1) / SPL;
   const int h = kh * (HEADS / KV_HEADS) + w4;
   const float2 cs = P.rope[(size_t)pos * 32 + lane];
@@ -646,7 +672,8 @@ __device__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm,
     sm.sq[w4][lane] = q0 * cs.x - q1 * cs.y;
     sm.sq[w4][lane + 32] = q0 * cs.y + q1 * cs.x;
   }
-  if (pos < t0 + SPL) {
+  if (c1 == nchunk) {
+    // this task reads the current position: write its K (normed, roped) and V
     const size_t off = ((size_t)kh * P.ctx + pos) * HEAD_DIM;
     if (w4 == 0) {
       float k0 = ldcg(qkv + DIM + kh * HEAD_DIM + lane), k1 = ldcg(qkv + DIM + kh * HEAD_DIM + lane + 32);
@@ -664,48 +691,72 @@ __device__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm,
     __threadfence();
   }
   group_sync(g);
-  const int tend = min(t0 + SPL, pos + 1), cnt = tend - t0;
-  {
-    const uint4* kg = (const uint4*)(S.kc + ((size_t)kh * P.ctx + t0) * HEAD_DIM);
-    const uint4* vg = (const uint4*)(S.vc + ((size_t)kh * P.ctx + t0) * HEAD_DIM);
+  const uint4* kg = (const uint4*)(S.kc + (size_t)kh * P.ctx * HEAD_DIM);
+  const uint4* vg = (const uint4*)(S.vc + (size_t)kh * P.ctx * HEAD_DIM);
+  // K/V rows of a chunk: 32 rows x 8 uint4 each, two per thread
+  uint4 kr[2], vr[2];
+  auto fetch = [&](int c) {
+    const int cnt = min(SPL, pos + 1 - c * SPL);
 #pragma unroll
     for (int i = 0; i < 2; i++) {
-      const int idx = gt + i * 128, r = idx >> 3, c = idx & 7;
+      const int idx = gt + i * 128, r = idx >> 3;
       if (r < cnt) {
-        *(uint4*)&sm.sk[r][c * 8] = __ldcg(kg + idx);
-        *(uint4*)&sm.sv[r][c * 8] = __ldcg(vg + idx);
+        kr[i] = __ldcg(kg + (size_t)c * SPL * 8 + idx);
+        vr[i] = __ldcg(vg + (size_t)c * SPL * 8 + idx);
       }
     }
-  }
-  group_sync(g);
-  float sc = -INFINITY;
-  if (lane < cnt) {
-    float acc = 0.f;
+  };
+  fetch(c0);
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
 #pragma unroll
-    for (int c8 = 0; c8 < 8; c8++) {
-      const uint4 v = *(const uint4*)&sm.sk[lane][c8 * 8];
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  for (int ci = 0; ci < ATTN_MAX_CPT; ci++) {
+    const int c = c0 + ci;
+    if (c >= c1) break;
+    const int cnt = min(SPL, pos + 1 - c * SPL);
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float2 f = __half22float2(*(const __half2*)&w[j]);
-        acc = fmaf(f.x, sm.sq[w4][c8 * 8 + 2 * j], acc);
-        acc = fmaf(f.y, sm.sq[w4][c8 * 8 + 2 * j + 1], acc);
+    for (int i = 0; i < 2; i++) {
+      const int idx = gt + i * 128, r = idx >> 3, cc = idx & 7;
+      if (r < cnt) {
+        *(uint4*)&sm.sk[r][cc * 8] = kr[i];
+        *(uint4*)&sm.sv[r][cc * 8] = vr[i];
       }
     }
-    sc = acc * 0.125f;
-  }
-  float m = sc;
+    if (c + 1 < c1) fetch(c + 1);
+    group_sync(g);
+    float sc = -INFINITY;
+    if (lane < cnt) {
+      float acc = 0.f;
 #pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  const float pl = lane < cnt ? expf(sc - m) : 0.f;
-  const float l = warp_sum(pl);
-  float o0 = 0.f, o1 = 0.f;
-  for (int t = 0; t < cnt; t++) {
-    const float pt = __shfl_sync(0xffffffffu, pl, t);
-    o0 = fmaf(pt, __half2float(sm.sv[t][lane]), o0);
-    o1 = fmaf(pt, __half2float(sm.sv[t][lane + 32]), o1);
+      for (int c8 = 0; c8 < 8; c8++) {
+        const uint4 v = *(const uint4*)&sm.sk[lane][c8 * 8];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float2 f = __half22float2(*(const __half2*)&w[q]);
+          acc = fmaf(f.x, sm.sq[w4][c8 * 8 + 2 * q], acc);
+          acc = fmaf(f.y, sm.sq[w4][c8 * 8 + 2 * q + 1], acc);
+        }
+      }
+      sc = acc * 0.125f;
+    }
+    float cm = sc;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    const float mn = fmaxf(m, cm);
+    const float scale = expf(m - mn);  // 0 on the first chunk (m = -inf, mn finite)
+    const float pl = lane < cnt ? expf(sc - mn) : 0.f;
+    l = fmaf(l, scale, warp_sum(pl));
+    o0 *= scale;
+    o1 *= scale;
+    for (int t = 0; t < cnt; t++) {
+      const float pt = __shfl_sync(0xffffffffu, pl, t);
+      o0 = fmaf(pt, __half2float(sm.sv[t][lane]), o0);
+      o1 = fmaf(pt, __half2float(sm.sv[t][lane + 32]), o1);
+    }
+    m = mn;
+    group_sync(g);  // the chunk's rows are read before the next chunk overwrites them
   }
-  float* pp = P.attn_part + (((size_t)kh * nsplit + split) * 4 + w4) * (HEAD_DIM + 2);
+  float* pp = P.attn_part + (((size_t)kh * nsplit + j) * 4 + w4) * (HEAD_DIM + 2);
   pp[lane] = o0;
   pp[lane + 32] = o1;
   if (lane == 0) {
@@ -716,23 +767,38 @@ __device__ void attn_task(const StepParams& P, const StepStage& S, AttnSmem& sm,
   group_sync(g);
   if (gt == 0) {
     __threadfence();
-    sm.last = atomicAdd(&P.ctl->attn_cnt[kh], 1u) == (unsigned)(nact - 1);
+    sm.last = atomicAdd(&P.ctl->attn_cnt[kh], 1u) == (unsigned)(ntask - 1);
   }
   group_sync(g);
   if (!sm.last) return;
   __threadfence();
+  // merge: lane s holds task s's statistics (ntask <= 32)
   const float* base = P.attn_part + ((size_t)kh * nsplit * 4 + w4) * (HEAD_DIM + 2);
-  float M = -INFINITY;
-  for (int sidx = lane; sidx < nact; sidx += 32) M = fmaxf(M, ldcg(base + (size_t)sidx * 4 * (HEAD_DIM + 2) + 64));
+  float ms = -INFINITY, ls = 0.f;
+  if (lane < ntask) {
+    ms = ldcg(base + (size_t)lane * PSTR + 64);
+    ls = ldcg(base + (size_t)lane * PSTR + 65);
+  }
+  float M = ms;
 #pragma unroll
   for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float L = 0.f, O0 = 0.f, O1 = 0.f;
-  for (int sidx = 0; sidx < nact; sidx++) {
-    const float* q = base + (size_t)sidx * 4 * (HEAD_DIM + 2);
-    const float w = expf(ldcg(q + 64) - M);
-    L = fmaf(ldcg(q + 65), w, L);
-    O0 = fmaf(ldcg(q + lane), w, O0);
-    O1 = fmaf(ldcg(q + lane + 32), w, O1);
+  const float ws = lane < ntask ? expf(ms - M) : 0.f;
+  const float L = warp_sum(ls * ws);
+  float O0 = 0.f, O1 = 0.f;
+  for (int s0 = 0; s0 < ntask; s0 += 8) {
+    float a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const bool in = s0 + i < ntask;
+      a[i] = in ? ldcg(base + (size_t)(s0 + i) * PSTR + lane) : 0.f;
+      b[i] = in ? ldcg(base + (size_t)(s0 + i) * PSTR + lane + 32) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float w = __shfl_sync(0xffffffffu, ws, (s0 + i) & 31);
+      O0 = fmaf(a[i], w, O0);
+      O1 = fmaf(b[i], w, O1);
+    }
   }
   S.out[h * HEAD_DIM + lane] = O0 / L;
   S.out[h * HEAD_DIM + lane + 32] = O1 / L;
@@ -825,14 +891,18 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
         }
         break;
       case ST_ATTN: {
-        const int nact = pos / ATTN_SPLIT + 1;
-        const int ntask = KV_HEADS * nact;
+        // at most 32 tasks per kv head (one merge statistic per lane), each
+        // covering cpt consecutive 32-position chunks
+        const int nchunk = pos / ATTN_SPLIT + 1;
+        const int cpt = (nchunk + 31) / 32;
+        const int nth = (nchunk + cpt - 1) / cpt;
+        const int ntask = KV_HEADS * nth;
         int a0, a1;
         tile_range(ntask, a0, a1);
         // two 4-warp groups (shared memory budget); the other warps idle here
         const int g = warp >> 2;
         if (g < 2)
-          for (int a = a0 + g; a < a1; a += 2) attn_task(P, S, stsm.attn[g], g, a / nact, a % nact, pos, nact);
+          for (int a = a0 + g; a < a1; a += 2) attn_task(P, S, stsm.attn[g], g, a / nth, a % nth, nth, cpt, pos);
         break;
       }
       case ST_QKV: ok = ring_stage<ST_QKV>(P, S, s, ring, full, empty, k, cs, stsm.xs); break;
