@@ -7,14 +7,15 @@
 // (monotonic arrival counters in global memory, acquire/release ordering,
 // bounded polling).
 //
-// Warp 8 of each CTA is a dedicated producer: it walks this CTA's weight
-// tiles of ALL stages in order and streams them through a 4-slot
+// Warp 16 (the last) of each CTA is a dedicated producer: it walks this CTA's
+// weight tiles of ALL stages in order and streams them through a 4-slot
 // shared-memory ring with bulk async copies (cp.async.bulk into this CTA only)
 // completed on mbarriers. It waits only for free ring slots and, before
-// routed-expert tiles, for the residual stage that publishes the router
-// partials; from those it computes the layer's top-4 experts itself (there is
-// no router stage). The weight stream of later stages is in flight while
-// earlier stages compute and the grid barriers never drain the HBM pipeline.
+// routed-expert tiles, for the layer's top-4 experts, which the consumers
+// compute at the start of the gate/up stage from the router partials the
+// residual stage publishes (there is no router stage). The weight stream of
+// later stages is in flight while earlier stages compute and the grid
+// barriers never drain the HBM pipeline.
 //
 // Warps 0-15 consume. Each holds the stage's activation unit in registers (one
 // 64-weight unit per lane, q6k.cuh layout) and computes one dot row of every
