@@ -147,17 +147,22 @@ __global__ void k_embed_n(Q6Mat E, const uint32_t* ids, float* x) {
 
 // RMSNorm of each token row (kernels.rs:576-634; lfm.rs:231-244).
 __global__ void __launch_bounds__(256) k_rmsnorm_n(const float* x, const float* w, float eps, float* out) {
+  static_assert(DIM == 2 * 4 * 256, "two float4 per thread");
   __shared__ float red[8];
-  const float* xr = x + (size_t)blockIdx.x * DIM;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < DIM; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  const float4* xr = (const float4*)(x + (size_t)blockIdx.x * DIM);
+  const float4 a = xr[threadIdx.x], b = xr[threadIdx.x + 256];
+  float ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, a.w * a.w)));
+  ss = fmaf(b.x, b.x, fmaf(b.y, b.y, fmaf(b.z, b.z, fmaf(b.w, b.w, ss))));
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float t = 0.f;
   for (int i = 0; i < 8; i++) t += red[i];
   const float inv = 1.0f / sqrtf(t / (float)DIM + eps);
-  for (int i = threadIdx.x; i < DIM; i += 256) out[(size_t)blockIdx.x * DIM + i] = xr[i] * inv * w[i];
+  const float4 wa = __ldg((const float4*)w + threadIdx.x), wb = __ldg((const float4*)w + threadIdx.x + 256);
+  float4* o = (float4*)(out + (size_t)blockIdx.x * DIM);
+  o[threadIdx.x] = make_float4(a.x * inv * wa.x, a.y * inv * wa.y, a.z * inv * wa.z, a.w * inv * wa.w);
+  o[threadIdx.x + 256] = make_float4(b.x * inv * wb.x, b.y * inv * wb.y, b.z * inv * wb.z, b.w * inv * wb.w);
 }
 
 // Short conv over n tokens (kernels/resident.rs:33-56: three taps over
@@ -472,31 +477,49 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(const float* x, int len, i
 }
 
 // Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574),
-// then route_n picks the top 4. One block per 8 tokens: 128-wide K chunks of
-// the token rows and the 32 router rows are staged in shared memory, and
-// thread (token t / 32, expert t % 32) accumulates its dot in K order.
+// then route_n picks the top 4. One block per 16 tokens: 128-wide K chunks of
+// the 32 router rows and the 16 token rows are staged in shared memory, and
+// thread (token pair t / 32, expert t % 32) accumulates its two dots in K order
+// (float4 reads: three shared loads per eight FMAs).
 __global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
-  constexpr int KC = 128, TOK = 8;
-  __shared__ float xs[TOK][KC], ws[N_EXPERT][KC + 1];
+  constexpr int KC = 128, TOK = 16, WS = KC + 4;  // WS: 16-byte skew per row, conflict-free float4 reads
+  __shared__ __align__(16) float xs[TOK][KC];
+  __shared__ __align__(16) float ws[N_EXPERT][WS];
   const int t = threadIdx.x, j0 = blockIdx.x * TOK;
-  const int tok = t >> 5, e = t & 31;
-  float acc = 0.f;
+  const int tp = t >> 5, e = t & 31;
+  float acc0 = 0.f, acc1 = 0.f;
   for (int k0 = 0; k0 < DIM; k0 += KC) {
-    for (int f = t; f < N_EXPERT * KC / 4; f += 256) {
-      const int r = f / (KC / 4), c4 = f % (KC / 4);
-      const float4 wv = *(const float4*)(Wr + (size_t)r * DIM + k0 + 4 * c4);
-      ws[r][4 * c4] = wv.x, ws[r][4 * c4 + 1] = wv.y, ws[r][4 * c4 + 2] = wv.z, ws[r][4 * c4 + 3] = wv.w;
-      if (r < TOK) {
-        const int j = min(j0 + r, n - 1);
-        *(float4*)&xs[r][4 * c4] = *(const float4*)(xn + (size_t)j * DIM + k0 + 4 * c4);
-      }
+#pragma unroll
+    for (int i = 0; i < N_EXPERT * KC / 4 / 256; i++) {
+      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
+      *(float4*)&ws[r][4 * c4] = __ldg((const float4*)(Wr + (size_t)r * DIM + k0) + c4);
+    }
+#pragma unroll
+    for (int i = 0; i < TOK * KC / 4 / 256; i++) {
+      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
+      const int j = min(j0 + r, n - 1);
+      *(float4*)&xs[r][4 * c4] = *((const float4*)(xn + (size_t)j * DIM + k0) + c4);
     }
     __syncthreads();
-#pragma unroll 16
-    for (int k = 0; k < KC; k++) acc = fmaf(ws[e][k], xs[tok][k], acc);
+#pragma unroll 8
+    for (int k4 = 0; k4 < KC / 4; k4++) {
+      const float4 w = *(const float4*)&ws[e][4 * k4];
+      const float4 x0 = *(const float4*)&xs[2 * tp][4 * k4];
+      const float4 x1 = *(const float4*)&xs[2 * tp + 1][4 * k4];
+      acc0 = fmaf(w.x, x0.x, acc0);
+      acc0 = fmaf(w.y, x0.y, acc0);
+      acc0 = fmaf(w.z, x0.z, acc0);
+      acc0 = fmaf(w.w, x0.w, acc0);
+      acc1 = fmaf(w.x, x1.x, acc1);
+      acc1 = fmaf(w.y, x1.y, acc1);
+      acc1 = fmaf(w.z, x1.z, acc1);
+      acc1 = fmaf(w.w, x1.w, acc1);
+    }
     __syncthreads();
   }
-  if (j0 + tok < n) logits[(size_t)(j0 + tok) * N_EXPERT + e] = acc;
+  const int ja = j0 + 2 * tp;
+  if (ja < n) logits[(size_t)ja * N_EXPERT + e] = acc0;
+  if (ja + 1 < n) logits[(size_t)(ja + 1) * N_EXPERT + e] = acc1;
 }
 
 // Router logits for few tokens (batched decode): one block per token, x
@@ -659,7 +682,7 @@ void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s) {
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
   static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
   if (n < 256) k_router_logits_tok<<<n, 256, 0, s>>>(Wr, xnorm, logits);  // few tokens: a block each
-  else k_router_logits_n<<<(n + 7) / 8, 256, 0, s>>>(Wr, xnorm, n, logits);
+  else k_router_logits_n<<<(n + 15) / 16, 256, 0, s>>>(Wr, xnorm, n, logits);
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {

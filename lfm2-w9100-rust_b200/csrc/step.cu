@@ -66,6 +66,9 @@ struct AttnSmem {
 // order: element (unit u, slot m*16+i) at xs[((m*4 + i/4) * U + u) * 4 + i%4],
 // so lane u's 16 float4 reads are consecutive across lanes (conflict-free).
 constexpr int XS_FLOATS = N_USED * EXPERT_FF;  // 7168: 4 expert vectors or one 7168 vector
+// the routed gate/up stage stages its 2048-float input here, above the router
+// partials (G x 33 floats + 33 sums fit below it for G <= 154 CTAs)
+constexpr int ROUTE_XOFF = XS_FLOATS - DIM;
 union StageSmem {
   AttnSmem attn[2];
   __align__(16) float xs[XS_FLOATS];
@@ -283,31 +286,49 @@ __device__ float route_layer(const StepParams& P, const float* bias, ConsShared&
   }
   cons_sync();
   // column sums in a fixed order: lane l adds CTAs l, l+32, ... then a fixed
-  // butterfly across the warp; warp w handles columns w, w+16, w+32
-  for (int e = warp; e < W; e += NCW) {
-    float v = 0.f;
-    for (int c = lane; c < G; c += 32) v += buf[c * W + e];
-    v = warp_sum(v);
-    if (lane == 0) buf[G * W + e] = v;
+  // butterfly across the warp; warp w handles columns w, w+16 (and warp 0
+  // column 32), the columns' chains interleaved
+  static_assert(W == 2 * NCW + 1, "33 columns over 16 warps");
+  {
+    const bool third = warp == 0;
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+    for (int c = lane; c < G; c += 32) {
+      v0 += buf[c * W + warp];
+      v1 += buf[c * W + warp + NCW];
+      if (third) v2 += buf[c * W + 2 * NCW];
+    }
+    v0 = warp_sum(v0);
+    v1 = warp_sum(v1);
+    if (third) v2 = warp_sum(v2);
+    if (lane == 0) {
+      buf[G * W + warp] = v0;
+      buf[G * W + warp + NCW] = v1;
+      if (third) buf[G * W + 2 * NCW] = v2;
+    }
   }
   cons_sync();
   if (warp == 0) {
     const float ss = buf[G * W + N_EXPERT];
     const float inv = 1.0f / sqrtf(ss / (float)DIM + P.eps);
     const float prob = 1.0f / (1.0f + expf(-(buf[G * W + lane] * inv)));
-    float score = prob + bias[lane];
+    // rank of this expert among the 32 (higher score first, lower index first
+    // among equal scores; a NaN score ranks last): the same order as picking
+    // the maximum four times, in one round of independent shuffles
+    const float s0 = prob + bias[lane];
+    const float score = s0 == s0 ? s0 : -INFINITY;
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const float o = __shfl_sync(0xffffffffu, score, j);
+      rank += (o > score || (o == score && j < lane)) ? 1 : 0;
+    }
     float ps[N_USED];
     int ids[N_USED];
 #pragma unroll
     for (int r = 0; r < N_USED; r++) {
-      float best = score;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
-      const unsigned mk = __ballot_sync(0xffffffffu, score == best);
-      const int id = mk ? __ffs(mk) - 1 : 0;
-      ps[r] = __shfl_sync(0xffffffffu, prob, id);
-      ids[r] = id;
-      if (lane == id) score = -INFINITY;
+      const unsigned mk = __ballot_sync(0xffffffffu, rank == r);  // the ranks are a permutation
+      ids[r] = __ffs(mk) - 1;
+      ps[r] = __shfl_sync(0xffffffffu, prob, ids[r]);
     }
     float sum = 0.f;
 #pragma unroll
@@ -322,9 +343,10 @@ __device__ float route_layer(const StepParams& P, const float* bias, ConsShared&
     __syncwarp();
     if (lane == 0) mbar_arrive(&cs.route_bar);  // release: psel/pselw are written
   }
-  const float ss_all = buf[gridDim.x * (N_EXPERT + 1) + N_EXPERT];
-  cons_sync();  // buf is reused by the activation staging
-  return ss_all;
+  // read by every consumer after the column-sum barrier; warp 0 may still be
+  // selecting experts from buf[G * W ...] when the caller stages its
+  // activation (above ROUTE_XOFF, clear of the partials)
+  return buf[G * W + N_EXPERT];
 }
 
 // The producer warp: all ring tiles of this CTA, in stage order (lane 0
@@ -427,7 +449,8 @@ __device__ __forceinline__ void stage_x(const StepParams& P, const StepStage& S,
       xr[4 * j + 3] = q.w;
     }
   }
-  cons_sync();  // xsm may be overwritten by the next stage's staging
+  // no barrier here: xsm is next written after the barrier that closes the
+  // stage's tile loop (cons_sync_or) or the next stage's opening barrier
 }
 
 // One weight-ring stage on the consumer side. Returns false on abort (agreed
@@ -472,18 +495,20 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
     const float4 g = __ldg((const float4*)S.norm + threadIdx.x);
     const float ss = route_layer(P, stage_table(ring)[S.dep].bias, cs, xsm);
     const float inv = 1.0f / sqrtf(ss / (float)DIM + P.eps);
-    *(float4*)&xsm[xs_index(4 * threadIdx.x, DIM / 64)] =
+    if ((int)gridDim.x * (N_EXPERT + 1) + N_EXPERT + 1 > ROUTE_XOFF) cons_sync();  // partials reach the staging
+    float* xst = xsm + ROUTE_XOFF;
+    *(float4*)&xst[xs_index(4 * threadIdx.x, DIM / 64)] =
         make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
     cons_sync();
 #pragma unroll
     for (int j = 0; j < 16; j++) {
-      const float4 q = *(const float4*)&xsm[(j * (DIM / 64) + u) * 4];
+      const float4 q = *(const float4*)&xst[(j * (DIM / 64) + u) * 4];
       xr[4 * j + 0] = q.x;
       xr[4 * j + 1] = q.y;
       xr[4 * j + 2] = q.z;
       xr[4 * j + 3] = q.w;
     }
-    cons_sync();
+    // no barrier here: xsm is next written after the stage's closing barrier
   } else {
     stage_x<TYPE>(P, S, cs, xsm, xr, u, vec);
   }

@@ -729,10 +729,13 @@ __global__ void k_tc_reduce(const float* part, int ksplit, int n, int rows, floa
 // Grouped layout from the expert lists (groups[e * (cap + 1)] = count, then
 // the selection slots): experts' rows start at tt-aligned bases; tiles =
 // {count, (expert, first row) ...}; slots[row] = selection slot or -1;
-// rowof[slot] = operand row. One block of 1024 threads: warp 0 scans the
-// counts, then every (expert, entry) pair is placed in one flat pass.
-__global__ void __launch_bounds__(1024) k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots,
-                                                         int* rowof, int nslots, int rpad, int tt) {
+// rowof[slot] = operand row (the caller clears rowof to -1 first). Every
+// block scans the 32 counts in warp 0, then the grid places the rows: row r
+// belongs to the expert whose padded range holds it and is either that
+// expert's entry r - base or padding. Each output word has one writer, so the
+// blocks need no ordering.
+__global__ void __launch_bounds__(256) k_tc_group_tiles(const int* groups, int cap, int* tiles, int* slots,
+                                                        int* rowof, int rpad, int tt) {
   __shared__ int base[N_EXPERT + 1], first[N_EXPERT + 1], tile0[N_EXPERT + 1];
   const int t = threadIdx.x, lane = t & 31;
   if (t < 32) {
@@ -754,28 +757,31 @@ __global__ void __launch_bounds__(1024) k_tc_group_tiles(const int* groups, int 
     if (lane == 0) base[0] = first[0] = tile0[0] = 0;
   }
   __syncthreads();
-  const int total = first[N_EXPERT];
-  if (t == 0) tiles[0] = tile0[N_EXPERT];
-  for (int i = t; i < tile0[N_EXPERT]; i += blockDim.x) {
+  const int gt = blockIdx.x * blockDim.x + t, gs = gridDim.x * blockDim.x;
+  const int ntiles = tile0[N_EXPERT], nrows = base[N_EXPERT];
+  if (gt == 0) tiles[0] = ntiles;
+  for (int i = gt; i < ntiles; i += gs) {
     int e = 0;
     while (tile0[e + 1] <= i) e++;
     tiles[1 + 2 * i] = e;
     tiles[2 + 2 * i] = base[e] + tt * (i - tile0[e]);
   }
-  for (int r = t; r < rpad; r += blockDim.x) slots[r] = -1;
-  for (int q = t; q < nslots; q += blockDim.x) rowof[q] = -1;
-  __syncthreads();
-  for (int f = t; f < total; f += blockDim.x) {
-    int lo = 0, hi = N_EXPERT - 1;  // expert e with first[e] <= f < first[e + 1]
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (first[mid] <= f) lo = mid;
-      else hi = mid - 1;
+  for (int r = gt; r < rpad; r += gs) {
+    int v = -1;
+    if (r < nrows) {
+      int lo = 0, hi = N_EXPERT - 1;  // the last expert e with base[e] <= r (empty experts share a base)
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (base[mid] <= r) lo = mid;
+        else hi = mid - 1;
+      }
+      const int i = r - base[lo];
+      if (i < first[lo + 1] - first[lo]) {
+        v = groups[(size_t)lo * (cap + 1) + 1 + i];
+        rowof[v] = r;
+      }
     }
-    const int e = lo, i = f - first[e];
-    const int slot = groups[(size_t)e * (cap + 1) + 1 + i];
-    slots[base[e] + i] = slot;
-    rowof[slot] = base[e] + i;
+    slots[r] = v;
   }
 }
 
@@ -976,7 +982,10 @@ cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, c
 cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s) {
   const int rpad = grouped_rpad(n);
   if (n <= 0 || (size_t)rpad > sc.rows || !sc.tiles || !sc.slots || !sc.rowof) return cudaErrorInvalidValue;
-  k_tc_group_tiles<<<1, 1024, 0, s>>>(groups, cap, sc.tiles, sc.slots, sc.rowof, n * N_USED, rpad, grouped_tt(n));
+  cudaError_t e = cudaMemsetAsync(sc.rowof, 0xFF, (size_t)n * N_USED * sizeof(int), s);  // rowof = -1
+  if (e != cudaSuccess) return e;
+  const int grid = std::min((rpad + 255) / 256, 148);
+  k_tc_group_tiles<<<grid, 256, 0, s>>>(groups, cap, sc.tiles, sc.slots, sc.rowof, rpad, grouped_tt(n));
   return cudaGetLastError();
 }
 
