@@ -366,8 +366,6 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
       mbar_init(&afull[s], 8);
       mbar_init(&aempty[s], 1);
     }
-    for (int r = 0; r < 2; r++) {
-    }
     for (int r = 0; r < RAWN; r++) {
       mbar_init(&raw_full[r], 1);
       mbar_init(&raw_empty[r], 8);
@@ -567,20 +565,39 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
     for (int i = LAG - 1; i >= 0; i--)
       if (ok && nbl - 1 - i >= 0) epilogue(nbl - 1 - i, dd[i]);
     if (ok) {
+      // Output rows of this thread's tokens, JC at a time: every load a chunk
+      // needs (scales, slots, residual values) is issued before its first
+      // store, so the chunk costs one memory round trip, not one per token.
       const int o = o0 + row;
+      const int bq = brow0 + TH * g;
+      constexpr int JC = TH < 16 ? TH : 16;
 #pragma unroll
-      for (int j = 0; j < TH; j++) {
-        const int br = brow0 + TH * g + j;
-        const float v = y[j] * __ldg(p.inv + br);
+      for (int j0 = 0; j0 < TH; j0 += JC) {
+        float v[JC];
+#pragma unroll
+        for (int j = 0; j < JC; j++) v[j] = __fmul_rn(y[j0 + j], __ldg(p.inv + bq + j0 + j));
         if (p.grouped) {
-          const int slot = __ldg(p.slots + br);
-          if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v;
+          int slot[JC];
+#pragma unroll
+          for (int j = 0; j < JC; j++) slot[j] = __ldg(p.slots + bq + j0 + j);
+#pragma unroll
+          for (int j = 0; j < JC; j++)
+            if (slot[j] >= 0) p.out[(size_t)slot[j] * p.ldo + o] = v[j];
         } else if (p.part) {
-          if (br < p.ntok) p.part[((size_t)blockIdx.z * p.ntok + br) * p.W.rows + o] = v;
-        } else if (br < p.ntok) {
-          float* dst = p.out + (size_t)br * p.ldo + o;
-          if (p.resid) *dst += v;
-          else *dst = v;
+#pragma unroll
+          for (int j = 0; j < JC; j++)
+            if (bq + j0 + j < p.ntok) p.part[((size_t)blockIdx.z * p.ntok + bq + j0 + j) * p.W.rows + o] = v[j];
+        } else if (p.resid) {
+          float old[JC];
+#pragma unroll
+          for (int j = 0; j < JC; j++) old[j] = bq + j0 + j < p.ntok ? p.out[(size_t)(bq + j0 + j) * p.ldo + o] : 0.f;
+#pragma unroll
+          for (int j = 0; j < JC; j++)
+            if (bq + j0 + j < p.ntok) p.out[(size_t)(bq + j0 + j) * p.ldo + o] = __fadd_rn(old[j], v[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < JC; j++)
+            if (bq + j0 + j < p.ntok) p.out[(size_t)(bq + j0 + j) * p.ldo + o] = v[j];
         }
       }
     }
