@@ -525,6 +525,8 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
   if (tr) cs.tw = cs.tc = 0;
   for (int t = t0; t < t1; t++, k++) {
     const int st = k % RING;
+    // the residual row this warp adds its dot to, loaded before the tile wait
+    const float rold = (TYPE == ST_RESID && lane == 0) ? S.resid[t * 16 + warp] : 0.f;
     if (tr) cs.ts = clock64();
     if (!ring_wait(&full[st], (k / RING) & 1, ctl)) {
       ok = false;
@@ -569,7 +571,7 @@ __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S,
         seg_src(S, cs.psel, t, 0, row0, ob);
         S.out[ob + row0 + warp] = acc0;
       } else if (TYPE == ST_RESID) {
-        S.resid[t * 16 + warp] += acc0;  // this warp owns the row
+        S.resid[t * 16 + warp] = rold + acc0;  // this warp owns the row
       } else if (TYPE == ST_LMHEAD) {
         const int row = t * 16 + warp;
         S.out[row] = acc0;
