@@ -480,27 +480,43 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(const float* x, int len, i
 // then route_n picks the top 4. One block per 16 tokens: 128-wide K chunks of
 // the 32 router rows and the 16 token rows are staged in shared memory, and
 // thread (token pair t / 32, expert t % 32) accumulates its two dots in K order
-// (float4 reads: three shared loads per eight FMAs).
+// (float4 reads: three shared loads per eight FMAs). The next chunk's global
+// loads are in flight while the current one is multiplied.
 __global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
   constexpr int KC = 128, TOK = 16, WS = KC + 4;  // WS: 16-byte skew per row, conflict-free float4 reads
+  constexpr int NW = N_EXPERT * KC / 4 / 256, NX = TOK * KC / 4 / 256;  // float4 loads per thread and chunk
   __shared__ __align__(16) float xs[TOK][KC];
   __shared__ __align__(16) float ws[N_EXPERT][WS];
   const int t = threadIdx.x, j0 = blockIdx.x * TOK;
   const int tp = t >> 5, e = t & 31;
+  float4 wr[NW], xr[NX];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < NW; i++) {
+      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
+      wr[i] = __ldg((const float4*)(Wr + (size_t)r * DIM + k0) + c4);
+    }
+#pragma unroll
+    for (int i = 0; i < NX; i++) {
+      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
+      xr[i] = *((const float4*)(xn + (size_t)min(j0 + r, n - 1) * DIM + k0) + c4);
+    }
+  };
+  fetch(0);
   float acc0 = 0.f, acc1 = 0.f;
   for (int k0 = 0; k0 < DIM; k0 += KC) {
 #pragma unroll
-    for (int i = 0; i < N_EXPERT * KC / 4 / 256; i++) {
-      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
-      *(float4*)&ws[r][4 * c4] = __ldg((const float4*)(Wr + (size_t)r * DIM + k0) + c4);
+    for (int i = 0; i < NW; i++) {
+      const int f = t + 256 * i;
+      *(float4*)&ws[f / (KC / 4)][4 * (f % (KC / 4))] = wr[i];
     }
 #pragma unroll
-    for (int i = 0; i < TOK * KC / 4 / 256; i++) {
-      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
-      const int j = min(j0 + r, n - 1);
-      *(float4*)&xs[r][4 * c4] = *((const float4*)(xn + (size_t)j * DIM + k0) + c4);
+    for (int i = 0; i < NX; i++) {
+      const int f = t + 256 * i;
+      *(float4*)&xs[f / (KC / 4)][4 * (f % (KC / 4))] = xr[i];
     }
     __syncthreads();
+    if (k0 + KC < DIM) fetch(k0 + KC);
 #pragma unroll 8
     for (int k4 = 0; k4 < KC / 4; k4++) {
       const float4 w = *(const float4*)&ws[e][4 * k4];
