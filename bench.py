@@ -351,6 +351,73 @@ def prefill_only(local: int, n: int) -> dict:
     return out
 
 
+def step_trace(local: int, n: int) -> dict:
+    """Stage timeline of the persistent decode step (profiling entry point):
+    an n-token prompt, 16 untimed decode steps, then one traced step of 8.
+    Per stage type: count, span per stage (first start to last arrival), the
+    median CTA's work, its staging prologue and wait for the first tile, the
+    grid-barrier gap before the stage; per tile: consumer warp 0's wait and
+    compute cycles. All times in microseconds."""
+    import torch
+
+    import lfm2_b200
+    torch.cuda.set_device(local)
+    eng = lfm2_b200.GpuEngine(model_path(0, None), local)
+    eng.set_ctx(4096)
+    p = prompt(n, 7)
+    first = int(np.argmax(eng.forward(p, 0)))
+    _, ms = eng.decode_loop(first, n, 16)
+    eng.step_trace(True)
+    eng.decode_loop(first, n, 8)
+    tr = eng.step_trace(False)
+    eng.close()
+    if tr is None:
+        return {"step_trace": "kernel chain decode path: no stage trace"}
+    import synth_gguf
+    types = ["EMBED"]
+    for layer in range(24):
+        types += ["QKV", "ATTN", "RESID"] if layer in synth_gguf.ATTN_LAYERS else ["CONV", "RESID"]
+        types += ["SWIGLU", "DOWN28"] if layer < 2 else ["XSWIGLU", "XDOWN"]
+    types.append("LMHEAD")
+    tr = tr.astype(np.int64)
+    ns, nc, _ = tr.shape
+    if len(types) != ns:
+        return {"step_trace": f"unexpected stage count {ns}"}
+    t0 = tr[0, :, 0].min()
+    start, staged, first_tile, done = (tr[:, :, i] - t0 for i in range(4))
+    agg, prev_end = {}, 0
+    for s_ in range(ns):
+        a = agg.setdefault(types[s_], {"count": 0, "span": 0.0, "work": 0.0, "prologue": 0.0, "first_tile": 0.0,
+                                       "gap": 0.0, "tiles": 0, "wait_cyc": 0, "compute_cyc": 0})
+        a["count"] += 1
+        a["span"] += (done[s_].max() - start[s_].min()) / 1e3
+        a["work"] += float(np.median(done[s_] - start[s_])) / 1e3
+        a["gap"] += (start[s_].min() - prev_end) / 1e3
+        prev_end = done[s_].max()
+        ok = tr[s_, :, 1] > 0
+        if ok.any():
+            a["prologue"] += float(np.median((staged[s_] - start[s_])[ok])) / 1e3
+            ok2 = tr[s_, :, 2] > 0
+            if ok2.any():
+                a["first_tile"] += float(np.median((first_tile[s_] - staged[s_])[ok2])) / 1e3
+        a["tiles"] += int(tr[s_, :, 5].sum())
+        a["wait_cyc"] += int(tr[s_, :, 4].sum())
+        a["compute_cyc"] += int(tr[s_, :, 6].sum())
+    table = {}
+    for k, a in sorted(agg.items(), key=lambda kv: -kv[1]["span"]):
+        c = a["count"]
+        row = {"count": c, "span_us": round(a["span"], 1), "per_stage_us": round(a["span"] / c, 2),
+               "work_us": round(a["work"] / c, 2), "prologue_us": round(a["prologue"] / c, 2),
+               "first_tile_us": round(a["first_tile"] / c, 2), "gap_us": round(a["gap"] / c, 2)}
+        if a["tiles"]:
+            row["tile_wait_cyc"] = round(a["wait_cyc"] / a["tiles"])
+            row["tile_compute_cyc"] = round(a["compute_cyc"] / a["tiles"])
+            row["tiles_per_cta"] = round(a["tiles"] / (c * nc), 1)
+        table[k] = row
+    return {"step_trace": {"prompt_len": n, "untraced_ms_per_step": round(ms / 15, 4),
+                           "traced_step_us": round(float(done.max()) / 1e3, 1), "ctas": int(nc), "stages": table}}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -365,6 +432,8 @@ def main():
     ap.add_argument("--sessions-only", action="store_true", help="only config 4 on this GPU (profiling entry point)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
                     help="only one warm-up and one timed N-token prefill (profiling entry point)")
+    ap.add_argument("--step-trace", type=int, default=0, metavar="N",
+                    help="only the decode step's stage timeline after an N-token prompt (profiling entry point)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local, pg = dist_setup(args.gpus)
@@ -375,6 +444,10 @@ def main():
     if args.prefill_only:
         if rank == 0:
             print(json.dumps(prefill_only(local, args.prefill_only)), flush=True)
+        return
+    if args.step_trace:
+        if rank == 0:
+            print(json.dumps(step_trace(local, args.step_trace)), flush=True)
         return
     if args.sessions_only:
         if rank == 0:
