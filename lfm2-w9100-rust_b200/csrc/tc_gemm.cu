@@ -342,6 +342,8 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
   __shared__ uint64_t bfull[BSTAGES], bempty[BSTAGES], afull[ASTAGES], aempty[ASTAGES], raw_full[RAWN],
       raw_empty[RAWN], acc_full[NACC], acc_empty[NACC], mma_done;
   __shared__ uint32_t tmem_base;
+  __shared__ float s_inv[TT];  // row scale of each operand row of the tile
+  __shared__ int s_slot[TT];   // grouped: output slot of each operand row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = p.W.nb;
   // this CTA's super-blocks [kb0, kb0 + nbl) (all of them unless split over K)
@@ -463,6 +465,14 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
     const int row = quarter * 32 + lane;
     const size_t wrow = (size_t)wrow0 + o0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(TH * g);
+    // the tile's row scales and slots, staged while the first operands load
+    // (the store phase then reads them from shared memory)
+    const int wt = threadIdx.x - 64;  // 0..255
+    if (wt < TT) {
+      s_inv[wt] = __ldg(p.inv + brow0 + wt);
+      s_slot[wt] = p.grouped ? __ldg(p.slots + brow0 + wt) : -1;
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight worker warps
     float y[TH];
 #pragma unroll
     for (int j = 0; j < TH; j++) y[j] = 0.f;
@@ -565,9 +575,9 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
     for (int i = LAG - 1; i >= 0; i--)
       if (ok && nbl - 1 - i >= 0) epilogue(nbl - 1 - i, dd[i]);
     if (ok) {
-      // Output rows of this thread's tokens, JC at a time: every load a chunk
-      // needs (scales, slots, residual values) is issued before its first
-      // store, so the chunk costs one memory round trip, not one per token.
+      // Output rows of this thread's tokens, JC at a time: a residual chunk's
+      // loads are all issued before its first store, so the chunk costs one
+      // memory round trip, not one per token.
       const int o = o0 + row;
       const int bq = brow0 + TH * g;
       constexpr int JC = TH < 16 ? TH : 16;
@@ -575,14 +585,13 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
       for (int j0 = 0; j0 < TH; j0 += JC) {
         float v[JC];
 #pragma unroll
-        for (int j = 0; j < JC; j++) v[j] = __fmul_rn(y[j0 + j], __ldg(p.inv + bq + j0 + j));
+        for (int j = 0; j < JC; j++) v[j] = __fmul_rn(y[j0 + j], s_inv[TH * g + j0 + j]);
         if (p.grouped) {
-          int slot[JC];
 #pragma unroll
-          for (int j = 0; j < JC; j++) slot[j] = __ldg(p.slots + bq + j0 + j);
-#pragma unroll
-          for (int j = 0; j < JC; j++)
-            if (slot[j] >= 0) p.out[(size_t)slot[j] * p.ldo + o] = v[j];
+          for (int j = 0; j < JC; j++) {
+            const int slot = s_slot[TH * g + j0 + j];
+            if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v[j];
+          }
         } else if (p.part) {
 #pragma unroll
           for (int j = 0; j < JC; j++)
