@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "dev_common.cuh"
+#include "host_once.h"
 #include "kernels.h"
 #include "tc_common.cuh"
 #include "tc_gemm.h"
@@ -324,8 +325,9 @@ cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, cons
   if (e != cudaSuccess) return e;
   e = tc_map_f16(&mv, vc, KV_HEADS * ctx, HEAD_DIM, KT);
   if (e != cudaSuccess) return e;
-  static std::once_flag once;
-  std::call_once(once, [] { cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ASMEM); });
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu, [] { cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ASMEM); });
   AttnParams p;
   p.q = q;
   p.q_stride = q_stride;

@@ -22,6 +22,7 @@
 #include <stdlib.h>
 
 #include "dev_common.cuh"
+#include "host_once.h"
 
 namespace lfm {
 namespace {
@@ -384,15 +385,15 @@ template <int MODE>
 void launch_mvt(const MvtParams& p, const LaunchCfg& c) {
   using TD = TileDef<MODE>;
   const size_t smem = TD::STAGES * stage_bytes_for(p.W.nb, TD::ROWS);
-  static bool attr = false;
-  if (!attr) {
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu, [] {
     cudaFuncSetAttribute(k_mvt<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)(TD::STAGES * stage_bytes_for(8, TD::ROWS)));
     // all of the unified L1/shared array as shared memory, so two CTAs (this
     // kernel and the next one under PDL) fit on an SM
     cudaFuncSetAttribute(k_mvt<MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr = true;
-  }
+  });
   // One or two CTAs per SM. Two hide more dependent-instruction latency (each
   // CTA keeps its own 3-4 stage weight ring) and pay off when every CTA has
   // many tiles (lm_head); for the short per-layer matrices one CTA per SM

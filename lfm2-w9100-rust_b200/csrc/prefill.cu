@@ -9,6 +9,7 @@
 // kernels/persistent.rs:58-76).
 #include <math.h>
 
+#include "host_once.h"
 #include "kernels.h"
 
 namespace lfm {
@@ -620,12 +621,12 @@ __global__ void k_add_n(float* x, const float* y, size_t count) {
 }  // namespace
 
 void gemm_q6_ld(const Q6Mat& W, const float* X, int n, float* out, int ldo, bool resid, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu, [] {
     cudaFuncSetAttribute(k_gemm_q6<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
     cudaFuncSetAttribute(k_gemm_q6<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
-    attr = true;
-  }
+  });
   dim3 grid((W.rows + GM - 1) / GM, (n + GN - 1) / GN);
   k_gemm_q6<false><<<grid, 256, GEMM_SMEM, s>>>(W, W.rows, X, n, W.nb * QK, 1, nullptr, 0, out, ldo, resid);
 }
@@ -636,11 +637,10 @@ void gemm_q6(const Q6Mat& W, const float* X, int n, float* out, bool resid, cuda
 
 void gemm_q6_grouped(const Q6Mat& W, int out_rows, const float* X, int x_div, const int* groups, int cap,
                      int max_count, float* out, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_gemm_q6<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM);
-    attr = true;
-  }
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu,
+                  [] { cudaFuncSetAttribute(k_gemm_q6<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM); });
   dim3 grid((out_rows + GM - 1) / GM, (max_count + GN - 1) / GN, N_EXPERT);
   k_gemm_q6<true><<<grid, 256, GEMM_SMEM, s>>>(W, out_rows, X, 0, W.nb * QK, x_div, groups, cap, out,
                                                out_rows, false);

@@ -32,6 +32,7 @@
 // returns.
 #include <math.h>
 
+#include <mutex>
 #include <string>
 
 #include "dev_common.cuh"
@@ -990,15 +991,24 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
 size_t step_smem_bytes() { return (size_t)RING * SLOT + (size_t)STEP_MAX_STAGES * sizeof(StepStage); }
 
 cudaError_t step_prepare() {
-  static cudaError_t status = cudaErrorNotReady;
-  if (status == cudaErrorNotReady) {
+  // kernel attributes and the residency check, once per device
+  static std::mutex mu;
+  static cudaError_t status[64];
+  static unsigned long long known = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!((known >> dev) & 1ull)) {
     cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes());
     cudaFuncSetAttribute(k_step, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     int blocks = 0;
-    status = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_step, NT, step_smem_bytes());
-    if (status == cudaSuccess && blocks < 1) status = cudaErrorCooperativeLaunchTooLarge;
+    cudaError_t st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_step, NT, step_smem_bytes());
+    if (st == cudaSuccess && blocks < 1) st = cudaErrorCooperativeLaunchTooLarge;
+    status[dev] = st;
+    known |= 1ull << dev;
   }
-  return status;
+  return status[dev];
 }
 
 std::string step_occupancy_report() {

@@ -28,6 +28,7 @@
 #include <mutex>
 
 #include "dev_common.cuh"
+#include "host_once.h"
 #include "tc_common.cuh"
 #include "tc_gemm.h"
 
@@ -275,9 +276,10 @@ constexpr int RAWH_BYTES = RAWH_Q + RAWH_S;   // 14 KB
 __host__ __device__ constexpr int q_off_b(int tt) { return q_astages(tt) * QA_BYTES; }
 constexpr int RAWN_MAX = 16;
 // Shared memory of the TT-token kernel: A ring, B ring of 2*TT-row chunks, and
-// as many raw half super-block buffers as fit (2 at TT = 128, 12 at TT = 16):
-// narrow tiles stream weights faster than they multiply, so they keep more
-// weight bytes in flight.
+// as many raw half super-block buffers as fit (2 at TT = 128 and at TT = 16,
+// which runs two CTAs per SM; 3 at TT = 64; 4 at TT = 32). The ring depths
+// were chosen by measurement: at TT = 128, A/B = 2/5 beat 3/4, 4/3, 3/3 and
+// 2/4 (the last three with deeper raw rings).
 __host__ __device__ constexpr int q_off_raw(int tt) { return q_off_b(tt) + q_bstages(tt) * 2 * tt * 128; }
 __host__ __device__ constexpr int q_smem_budget(int tt) { return q_ctas_per_sm(tt) == 2 ? 110 * 1024 : 232448 - 2048; }
 __host__ __device__ constexpr int q_rawn(int tt) {
@@ -857,8 +859,9 @@ cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, f
   e = tc_map_f16(&mb, B, N, K, TN);
   if (e != cudaSuccess) return e;
   const int smem = STAGES * STAGE_BYTES + 1024;
-  static std::once_flag once;
-  std::call_once(once, [smem] { cudaFuncSetAttribute(k_tc_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu, [smem] { cudaFuncSetAttribute(k_tc_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
   k_tc_f16<<<dim3(M / TM, N / TN), THREADS, smem, s>>>(ma, mb, C, M, N, K, err);
   return cudaGetLastError();
 }
@@ -871,8 +874,10 @@ cudaError_t tc_gemm_f16_bmn(const __half* A, const __half* B, int M, int K, floa
   if (e != cudaSuccess) return e;
   e = tc_map_f16(&mb, B, K, BN_N, TK);  // B [K][64]: 64-wide rows, 64-row boxes
   if (e != cudaSuccess) return e;
-  static std::once_flag once;
-  std::call_once(once, [] { cudaFuncSetAttribute(k_tc_f16_bmn, cudaFuncAttributeMaxDynamicSharedMemorySize, BMN_SMEM); });
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu,
+                  [] { cudaFuncSetAttribute(k_tc_f16_bmn, cudaFuncAttributeMaxDynamicSharedMemorySize, BMN_SMEM); });
   k_tc_f16_bmn<<<M / TM, THREADS, BMN_SMEM, s>>>(ma, mb, C, M, K, err);
   return cudaGetLastError();
 }
@@ -923,10 +928,10 @@ bool fits(const TcScratch& sc, int rpad, int K) {
 template <int TT>
 cudaError_t launch_q6_tt(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mx, dim3 grid,
                          const TcQ6Params& p, cudaStream_t s) {
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(k_tc_q6<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, q_smem(TT));
-  });
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu,
+                  [] { cudaFuncSetAttribute(k_tc_q6<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, q_smem(TT)); });
   k_tc_q6<TT><<<grid, QTHREADS, q_smem(TT), s>>>(mq, ms, mx, p);
   return cudaGetLastError();
 }
