@@ -159,10 +159,12 @@ def barrier(pg):
 
 
 def reduce_max(pg, v: float) -> float:
+    """Max of v over the ranks (the job's time is its slowest rank's)."""
     if pg is None:
         return v
     import torch
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cpu" if pg.get_backend() == "gloo" else "cuda"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     return float(t.item())
 
