@@ -50,7 +50,9 @@ def q6_bytes(in_dim, out_dim):
 
 
 def decode_bytes_per_token(ctx_len: float) -> dict:
-    """Algorithmic HBM bytes of one decode token."""
+    """Algorithmic HBM bytes of one decode token (config 2): every dense Q6_K
+    matrix once, the 4 routed experts of each MoE layer, the tied lm_head, the
+    f32 routers, the fp16 K/V read up to ctx_len and the small f32 tensors."""
     attn = q6_bytes(DIM, DIM) * 2 + q6_bytes(DIM, 512) * 2
     conv = q6_bytes(DIM, 3 * DIM) + q6_bytes(DIM, DIM)
     dense = q6_bytes(DIM, 7168) * 2 + q6_bytes(7168, DIM)
@@ -64,7 +66,9 @@ def decode_bytes_per_token(ctx_len: float) -> dict:
 
 
 def prefill_flops(n: int) -> float:
-    """Algorithmic FLOPs of an n-token prefill."""
+    """Algorithmic FLOPs of an n-token prefill (config 3): the Q6_K projections
+    of every token (4 routed experts per MoE layer), causal attention, and the
+    lm_head for the last token only."""
     mac_tok = (N_ATTN * (DIM * DIM * 2 + DIM * 512 * 2) + N_CONV * (DIM * 3 * DIM + DIM * DIM)
                + N_DENSE * 3 * DIM * 7168 + N_MOE * 4 * 3 * DIM * 1792)
     attn = N_ATTN * 4 * 32 * 64 * (n * (n + 1) / 2)

@@ -4,8 +4,8 @@
 
 Sources under csrc/ are compiled with nvcc
 (-gencode arch=compute_100a,code=sm_100a) into _build/ and linked into
-lfm2-w9100-rust_b200/liblfm2_b200.so, which travels with the repository
-snapshot (it is git-ignored, not gpurun-ignored).
+lfm2-w9100-rust_b200/liblfm2_b200.so, next to the Python binding that loads
+it (the library is a build output and is not committed).
 """
 
 from __future__ import annotations
