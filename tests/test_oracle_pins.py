@@ -182,3 +182,25 @@ def test_f16_rne_matches_reference_integer_rounding(oracle_mod):
         assert got == _half_round_bits(x), hex(b)
         # and IEEE RNE as numpy implements it
         assert got == int(np.array([x], dtype=np.float32).astype(np.float16).view(np.uint16)[0]), hex(b)
+
+
+def test_threaded_matmul_is_bit_identical_to_one_thread(oracle_mod):
+    # The CPU baseline runs the oracle on every host core; threads split output
+    # rows only, so each row's sum keeps its order and the results must not
+    # change with the thread count.
+    rng = np.random.default_rng(5)
+    in_dim, out_dim, n = 2048, 256, 3
+    w = rng.integers(0, 256, out_dim * (in_dim // 256) * 210, dtype=np.uint8).reshape(-1, 210)
+    w[:, 208], w[:, 209] = 0x00, 0x1C  # small fp16 d
+    x = rng.standard_normal(in_dim * n).astype(np.float32)
+    L = oracle_mod.lib()
+    before = L.oracle_num_threads()
+    try:
+        L.oracle_set_threads(1)
+        one = oracle_mod.q6k_matmul_f32(w.ravel(), in_dim, out_dim, x, n)
+        L.oracle_set_threads(4)
+        four = oracle_mod.q6k_matmul_f32(w.ravel(), in_dim, out_dim, x, n)
+    finally:
+        L.oracle_set_threads(before)
+    assert np.isfinite(one).all()
+    assert np.array_equal(one, four)
