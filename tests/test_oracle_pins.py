@@ -204,3 +204,26 @@ def test_threaded_matmul_is_bit_identical_to_one_thread(oracle_mod):
         L.oracle_set_threads(before)
     assert np.isfinite(one).all()
     assert np.array_equal(one, four)
+
+
+def _rank_top4(score):
+    """The decode step's selection rule, restated: every expert's rank is the
+    number of experts with a higher score plus the lower-indexed experts with
+    an equal one (a NaN score ranks last); ranks 0..3 are picked in order."""
+    s = np.where(np.isnan(score), -np.inf, score).astype(np.float32)
+    n = s.size
+    rank = [int(np.sum(s > s[i]) + np.sum(s[:i] == s[i])) for i in range(n)]
+    assert sorted(rank) == list(range(n))  # a permutation: one expert per rank
+    return [rank.index(r) for r in range(4)]
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_one_round_rank_selection_matches_reference_top4(oracle_mod, seed):
+    # kernels/resident.rs:58-99: highest score first, the lower index first
+    # among equal scores. Logits on a coarse grid make many exact ties.
+    rng = np.random.default_rng(seed)
+    lg = (rng.integers(-8, 9, 32) / 4.0).astype(np.float32)
+    bias = np.zeros(32, dtype=np.float32) if seed % 2 == 0 else (rng.integers(-4, 5, 32) / 16.0).astype(np.float32)
+    p = (1.0 / (1.0 + np.exp(-lg))).astype(np.float32)
+    sel, _ = oracle_mod.route(lg, bias)
+    assert _rank_top4(p + bias) == list(sel)
