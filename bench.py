@@ -38,9 +38,10 @@ METRIC = "decode tok/s bs1 @512 ctx; prefill tok/s @3840; % of HBM/tensor roofli
 PROMPT_LEN = 512
 PREFILL_LEN = 3840
 SEED = 1234
-# DRAM bytes (read + write) of one decode step from an ncu capture of the same
-# workload (profiles/ holds the capture summary); keyed by decode path.
-TRAFFIC: dict = {"persistent-step": 1442.7e6}
+# DRAM bytes (read + write) of one decode step, taken from an ncu capture of
+# the same workload (not measured by this run); keyed by decode path, with the
+# profile summary that holds the capture.
+TRAFFIC: dict = {"persistent-step": (1442.7e6, "profiles/k_step_decode_config2.md")}
 DIM, VOCAB = 2048, 128000
 N_ATTN, N_CONV, N_DENSE, N_MOE = 6, 18, 2, 22
 
@@ -198,47 +199,78 @@ def microbench(device: int) -> list:
     torch.cuda.set_device(device)
     s = torch.cuda.current_stream()
     out = []
-    shapes = [("lm_head 2048->128000", 2048, 128000, 1), ("lm_head 2048->65536", 2048, 65536, 1),
-              ("attn/conv 2048->2048", 2048, 2048, 1), ("conv in_proj 2048->6144", 2048, 6144, 1),
-              ("dense gate 2048->7168", 2048, 7168, 1), ("expert gate/up 2048->1792 x4", 2048, 1792, 4),
-              ("expert down 1792->2048 x4", 1792, 2048, 4)]
-    for name, ind, outd, mult in shapes:
-        nbytes = lib.lfm_q6k_device_bytes(ind, outd)
-        copies = max(1, int(np.ceil(512e6 / nbytes)))
+    peak = measured_peaks()["hbm_gbs"]
+    # (name, in, out, routed experts): routed rows run lfm_q6k_routed on a
+    # 32-expert matrix with 4 selected experts, the decode's q6k_routed
+    # (resident_graph.rs:446-495); their bytes count all 4 experts.
+    shapes = [("lm_head 2048->128000", 2048, 128000, 0), ("lm_head 2048->65536", 2048, 65536, 0),
+              ("attn/conv 2048->2048", 2048, 2048, 0), ("attn k/v 2048->512", 2048, 512, 0),
+              ("conv in_proj 2048->6144", 2048, 6144, 0), ("dense gate/up 2048->7168", 2048, 7168, 0),
+              ("dense down 7168->2048", 7168, 2048, 0),
+              ("routed gate/up 2048->1792 x4 of 32 experts", 2048, 1792, 4),
+              ("routed down 1792->2048 x4 of 32 experts", 1792, 2048, 4)]
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    st = ctypes.c_void_p(s.cuda_stream)
+    for name, ind, outd, routed in shapes:
+        mrows = outd * 32 if routed else outd
+        nbytes = lib.lfm_q6k_device_bytes(ind, mrows)
+        copies = max(2 if routed else 1, int(np.ceil(512e6 / nbytes)))
         g = torch.Generator(device="cuda").manual_seed(1)
         pool = [torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
         for w in pool:  # plausible fp16 d values: clear the top exponent bits
             w.view(-1)[-(nbytes // 105):].bitwise_and_(0x3B)
-        x = torch.randn(ind, device="cuda")
-        y = torch.empty(outd, device="cuda")
-        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        if routed:
+            # 8 disjoint groups of 4 experts, rotated with the copies: each
+            # (copy, group) pair recurs only after copies*8 calls (> L2)
+            ids = torch.arange(32, dtype=torch.int32, device="cuda").view(8, 4)[torch.tensor([0, 5, 2, 7, 4, 1, 6, 3])]
+            ids = ids.contiguous()
+            x = torch.randn(4 * ind, device="cuda")
+            y = torch.empty(4 * outd, device="cuda")
+            xs = ind if ind == 1792 else 0  # down: one input per slot; gate/up: a shared input
+            cycle = copies * 8
+
+            def call(i):
+                return lib.lfm_q6k_routed(P(pool[i % copies]), ind, outd, 32, P(ids[(i // copies) % 8]), P(x), xs,
+                                          P(y), st)
+        else:
+            x = torch.randn(ind, device="cuda")
+            y = torch.empty(outd, device="cuda")
+            cycle = copies
+
+            def call(i):
+                return lib.lfm_q6k_matmul(P(pool[i % copies]), ind, outd, P(x), 1, P(y), st)
         for i in range(3):
-            lib.lfm_q6k_matmul(P(pool[i % copies]), ind, outd, P(x), 1, P(y), ctypes.c_void_p(s.cuda_stream))
-        iters = max(20, copies)
+            lfm2_b200.ops_check(call(i), name)
+        iters = max(20, cycle)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(s)
         for i in range(iters):
-            lib.lfm_q6k_matmul(P(pool[i % copies]), ind, outd, P(x), 1, P(y), ctypes.c_void_p(s.cuda_stream))
+            call(i)
         e1.record(s)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000 / iters
-        alg = q6_bytes(ind, outd) + 4 * ind + 4 * outd
-        out.append({"shape": name, "us_per_matvec": round(us, 2), "gb_s": round(alg / us / 1e3, 1),
-                    "x_per_token": mult})
+        k = routed or 1
+        alg = k * (q6_bytes(ind, outd) + 4 * outd) + (k if ind == 1792 and routed else 1) * 4 * ind
+        out.append({"shape": name, "us_per_call": round(us, 2), "bytes": int(alg), "gb_s": round(alg / us / 1e3, 1),
+                    "frac": round(alg / us / 1e3 / peak, 4)})
         del pool
         torch.cuda.empty_cache()
     return out
 
 
-def cpu_baseline(path: str, steps: int, warmup: int, threads: int | None = None) -> dict:
-    """The oracle on the host cores: 512-token prefill (untimed), then greedy
-    decode steps at 512+ context (timed)."""
+def cpu_baseline(path: str, steps: int, warmup: int, threads: int | None = None, one_core_steps: int = 3) -> dict:
+    """The oracle on the host cores: 512-token prefill (untimed setup), `warmup`
+    untimed and `steps` timed greedy decode steps at 512+ context on `threads`
+    threads; then the first `one_core_steps` of those steps again from the
+    same state on ONE thread (the reference's Engine is single-threaded,
+    lfm.rs:290-694), whose logits must be bit-identical to the threaded run's;
+    and config 0's 16-token prefill timed on both thread counts."""
     import oracle
     oracle.build()
-    if threads:
-        os.environ["OMP_NUM_THREADS"] = str(threads)
-        oracle.lib().oracle_set_threads(threads)
+    threads = threads or len(os.sched_getaffinity(0))
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    oracle.lib().oracle_set_threads(threads)
     o = oracle.OracleEngine(path, kv_f16=True)
     cores = oracle.lib().oracle_num_threads()
     o.set_ctx(4096)
@@ -251,32 +283,66 @@ def cpu_baseline(path: str, steps: int, warmup: int, threads: int | None = None)
     for _ in range(warmup):
         tok = int(np.argmax(o.forward(np.array([tok], np.uint32), pos)))
         pos += 1
+    o.checkpoint()
+    tok0, pos0, kept = tok, pos, []
     t0 = time.perf_counter()
-    for _ in range(steps):
-        tok = int(np.argmax(o.forward(np.array([tok], np.uint32), pos)))
+    for i in range(steps):
+        lg = o.forward(np.array([tok], np.uint32), pos)
+        if i < one_core_steps:
+            kept.append(lg.copy())
+        tok = int(np.argmax(lg))
         pos += 1
     dt = time.perf_counter() - t0
+    # the same steps on one thread, from the same state
+    o.rollback()
+    oracle.lib().oracle_set_threads(1)
+    tok, pos, same = tok0, pos0, True
+    n1 = min(one_core_steps, steps)
+    t0 = time.perf_counter()
+    for i in range(n1):
+        lg = o.forward(np.array([tok], np.uint32), pos)
+        same = same and np.array_equal(lg.view(np.uint32), kept[i].view(np.uint32))
+        tok = int(np.argmax(lg))
+        pos += 1
+    dt1 = time.perf_counter() - t0
+    p16 = prompt(16, 0)
+    t0 = time.perf_counter()
+    o.forward(p16, 0)
+    pf1 = time.perf_counter() - t0
+    oracle.lib().oracle_set_threads(threads)
+    t0 = time.perf_counter()
+    o.forward(p16, 0)
+    pfn = time.perf_counter() - t0
     o.close()
     return {"value": round(steps / dt, 3), "unit": "tok/s", "cores": cores, "kind": "port",
             "sample": f"{steps} greedy decode tokens after a {PROMPT_LEN}-token prefill (prefill "
                       f"{PROMPT_LEN / prefill_s:.1f} tok/s), synthetic model, f16 K/V, {cores} threads",
-            "prefill_tok_s": round(PROMPT_LEN / prefill_s, 2)}
+            "prefill_tok_s": round(PROMPT_LEN / prefill_s, 2), "nproc": os.cpu_count(),
+            "prefill16_tok_s": round(16 / pfn, 2),
+            "one_core": {"decode_tok_s": round(n1 / dt1, 4), "steps": n1, "prefill16_tok_s": round(16 / pf1, 3),
+                         "bit_identical_to_threaded": bool(same),
+                         "sample": f"the first {n1} of the timed decode steps again from the same state on "
+                                   "1 thread; a 16-token prompt (config 0 shape) on 1 thread"}}
+
+
+def workload_config(ws: int) -> dict:
+    """`config` of both arms' JSON lines (the same workload)."""
+    return {"workload": "config 2: 512-token seeded prompt, greedy bs1 decode", "prompt_len": PROMPT_LEN,
+            "ctx": 4096, "parallelism": f"replicas x{ws}",
+            "l2": "no flush needed: every step streams ~1.4 GB of weights (> 126 MB L2)"}
 
 
 def run_reference(args, ws, rank, pg):
     if rank != 0:
         return
     path = model_path(0, None)
-    steps = min(args.steps, 32)
-    warm = min(args.warmup, 3)
     # all the host threads this process may use (torchrun sets OMP_NUM_THREADS=1)
-    cb = cpu_baseline(path, steps, warm, threads=len(os.sched_getaffinity(0)))
+    cb = cpu_baseline(path, args.steps, args.warmup, threads=len(os.sched_getaffinity(0)))
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / cb["value"], 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic seeded random-init Q6_K weights of the exact architecture",
-            "config": {"workload": "config 2: 512-token seeded prompt, greedy bs1 decode", "prompt_len": PROMPT_LEN,
-                       "parallelism": "host cores"},
+            "config": workload_config(args.gpus),
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -529,8 +595,10 @@ def main():
     path_name = info["decode_path"]
     kernel = ("k_step: one persistent cooperative kernel per decode token" if path_name == "persistent-step"
               else f"decode step as a CUDA graph of {info['launches_per_decode']} kernels")
+    traffic, traffic_src = TRAFFIC.get(path_name, (None, None))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": TRAFFIC.get(path_name),
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "traffic_source": traffic_src and f"ncu capture summarised in {traffic_src}, not measured by this run",
                 "kernel": kernel, "bytes_per_step": int(bpt["total"]),
                 "peak_source": peaks["source"]}
 
@@ -572,10 +640,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic seeded random-init Q6_K weights of the exact architecture",
-                "config": {"workload": "config 2: 512-token seeded prompt, greedy bs1 decode",
-                           "prompt_len": PROMPT_LEN, "ctx": 4096, "parallelism": f"replicas x{ws}",
-                           "decode_path": path_name,
-                           "l2": "no flush needed: every step streams ~1.4 GB of weights (> 126 MB L2)"},
+                "config": workload_config(ws), "decode_path": path_name,
                 "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "prefill": prefill, "multi_session": multi, "microbench": micro, "cpu_baseline": cpu,
                 "tokens_head": toks[:8]}

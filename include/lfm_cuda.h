@@ -68,6 +68,15 @@ typedef struct lfm_counters {
 
 /* ---- engine lifetime ------------------------------------------------- */
 
+/* The model check of GpuEngine::load without a device: parse the GGUF header
+ * with the reference parser's rules (parser::gguf::parse,
+ * parser/src/gguf.rs:304-440), read and validate the hyperparameters
+ * (load_hyperparams, lfm.rs:102-145) and check that every tensor the engine
+ * loads exists with its GGML type and shape. Reads no tensor payload.
+ * LFM_ERR_MODEL with the message in lfm_global_error on any violation;
+ * `out` (may be null) receives the hyperparameters. */
+lfm_status lfm_model_inspect(const char* gguf_path, lfm_hparams* out);
+
 /* GpuEngine::load(&ModelFile) (gpu_lfm.rs:51-115): parse the GGUF, validate
  * geometry (lfm.rs:115-126), repack every Q6_K tensor into the device layout
  * and upload it. `device` is the CUDA ordinal. */
@@ -230,9 +239,11 @@ lfm_status lfm_argmax(const float* x_dev, uint32_t n, uint32_t* out_dev, void* s
  * lfm_argmax; n must be 1..2^30 (larger n returns LFM_ERR_ARG with a message
  * in lfm_ops_error). The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress), so make that first call before any stream
- * capture. All calls on a device share the one array: calls that overlap on
- * the GPU (different streams, no ordering between them) race and may return
- * wrong indices. */
+ * capture. The address is cached per device together with the context it
+ * belongs to; after a device reset the next call looks it up again. All
+ * calls on a device share the one array: calls that overlap on the GPU
+ * (different streams, no ordering between them) race and may return wrong
+ * indices. */
 lfm_status lfm_argmax_noalloc(const float* x_dev, uint32_t n, uint32_t* out_dev, void* stream);
 
 /* Tensor-core GEMM core of the prompt path (tcgen05 MMA, fp32 accumulation in

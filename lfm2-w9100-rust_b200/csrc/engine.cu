@@ -89,6 +89,7 @@ struct BatchState {
   int* next = nullptr;
   float* logits = nullptr;              // [session][vocab]
   float* attn_part = nullptr;           // attention split partials of one step
+  uint32_t last_count = 0;              // entries of the last lfm_batch_decode step
   std::vector<int> h_map;
   std::vector<void*> allocs;
 };
@@ -279,13 +280,11 @@ const float* EngineImpl::upload_f32(const GgufFile& f, const GgufTensor& t) {
   return (const float*)d;
 }
 
-bool EngineImpl::load(const char* path) {
-  GgufFile f;
-  if (!f.open(path)) {
-    set_err(this, "parse GGUF header: " + f.err());
-    return false;
-  }
-  // load_hyperparams (lfm.rs:102-145)
+// load_hyperparams (lfm.rs:102-145): the metadata keys, the reference's
+// hard-coded geometry check and its message, plus the limits of this engine
+// (short-conv L_cache 3, dense n_ff 7168, 8 KV heads per attention layer).
+// Needs no device.
+static bool read_hparams(const GgufFile& f, lfm_hparams& hp, std::string& err) {
   uint32_t nl, dim, heads, vocab, ne, nu, eff, nff;
   std::vector<uint32_t> kvh;
   const char* keys[] = {"lfm2moe.block_count", "lfm2moe.embedding_length", "lfm2moe.attention.head_count",
@@ -294,11 +293,11 @@ bool EngineImpl::load(const char* path) {
   uint32_t* outs[] = {&nl, &dim, &heads, &vocab, &ne, &nu, &eff, &nff};
   for (int i = 0; i < 8; i++)
     if (!f.meta_u32(keys[i], *outs[i])) {
-      set_err(this, std::string("metadata ") + keys[i] + " not a u32");
+      err = std::string("metadata ") + keys[i] + " not a u32";
       return false;
     }
   if (!f.meta_u32_array("lfm2moe.attention.head_count_kv", kvh)) {
-    set_err(this, "metadata lfm2moe.attention.head_count_kv not an array");
+    err = "metadata lfm2moe.attention.head_count_kv not an array";
     return false;
   }
   if (dim != DIM || heads != HEADS || nl != 24 || vocab != 128000 || ne != N_EXPERT || nu != N_USED ||
@@ -307,13 +306,14 @@ bool EngineImpl::load(const char* path) {
     snprintf(b, sizeof b,
              "unsupported geometry: dim=%u heads=%u layers=%u vocab=%u n_expert=%u n_used=%u expert_ff=%u", dim,
              heads, nl, vocab, ne, nu, eff);
-    set_err(this, b);
+    err = b;
     return false;
   }
   if (kvh.size() != nl) {
-    set_err(this, "head_count_kv length differs from block_count");
+    err = "head_count_kv length differs from block_count";
     return false;
   }
+  hp = lfm_hparams{};
   hp.dim = dim;
   hp.heads = heads;
   hp.head_dim = HEAD_DIM;
@@ -326,21 +326,80 @@ bool EngineImpl::load(const char* path) {
   hp.dense_lead = f.meta_u32_default("lfm2moe.leading_dense_block_count", 2);
   hp.conv_l_cache = f.meta_u32_default("lfm2moe.shortconv.l_cache", 3);
   hp.eos = f.meta_u32_default("tokenizer.ggml.eos_token_id", 124900);
-  if (!f.meta_f32("lfm2moe.attention.layer_norm_rms_epsilon", hp.eps) ||
-      !f.meta_f32("lfm2moe.rope.freq_base", hp.rope_theta)) {
-    set_err(this, "metadata eps / rope.freq_base not an f32");
+  if (!f.meta_f32("lfm2moe.attention.layer_norm_rms_epsilon", hp.eps)) {
+    err = "metadata lfm2moe.attention.layer_norm_rms_epsilon not an f32";
+    return false;
+  }
+  if (!f.meta_f32("lfm2moe.rope.freq_base", hp.rope_theta)) {
+    err = "metadata lfm2moe.rope.freq_base not an f32";
     return false;
   }
   for (uint32_t l = 0; l < nl; l++) hp.kv_heads[l] = kvh[l];
   if (hp.conv_l_cache != 3 || nff != N_FF || hp.dense_lead > nl) {
-    set_err(this, "unsupported short-conv / dense FFN geometry");
+    err = "unsupported short-conv / dense FFN geometry";
     return false;
   }
   for (uint32_t l = 0; l < nl; l++)
     if (kvh[l] != 0 && kvh[l] != KV_HEADS) {
-      set_err(this, "attention layers must have 8 KV heads");
+      err = "attention layers must have 8 KV heads";
       return false;
     }
+  return true;
+}
+
+// Every tensor the engine uploads, with its GGML type and dimensions (the
+// names and shapes of the reference's loader, lfm.rs:147-190 and
+// gpu_lfm.rs:51-115). Reads no payload and needs no device.
+static bool check_tensors(const GgufFile& f, const lfm_hparams& hp, std::string& err) {
+  auto need = [&](const std::string& name, uint32_t type, std::vector<uint64_t> ne_) {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) {
+      err = "missing tensor " + name;
+      return false;
+    }
+    if (t->type != type || t->ne != ne_) {
+      err = "tensor " + name + " has unexpected type/shape";
+      return false;
+    }
+    return true;
+  };
+  if (!need("token_embd.weight", 14, {DIM, hp.vocab}) || !need("token_embd_norm.weight", 0, {DIM})) return false;
+  for (uint32_t l = 0; l < hp.n_layers; l++) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    if (!need(p + "attn_norm.weight", 0, {DIM}) || !need(p + "ffn_norm.weight", 0, {DIM})) return false;
+    bool ok = hp.kv_heads[l] > 0
+                  ? need(p + "attn_q.weight", 14, {DIM, DIM}) && need(p + "attn_k.weight", 14, {DIM, 512}) &&
+                        need(p + "attn_v.weight", 14, {DIM, 512}) && need(p + "attn_output.weight", 14, {DIM, DIM}) &&
+                        need(p + "attn_q_norm.weight", 0, {HEAD_DIM}) && need(p + "attn_k_norm.weight", 0, {HEAD_DIM})
+                  : need(p + "shortconv.in_proj.weight", 14, {DIM, 3 * DIM}) &&
+                        need(p + "shortconv.out_proj.weight", 14, {DIM, DIM}) &&
+                        need(p + "shortconv.conv.weight", 0, {3, DIM});
+    if (!ok) return false;
+    ok = l < hp.dense_lead
+             ? need(p + "ffn_gate.weight", 14, {DIM, N_FF}) && need(p + "ffn_up.weight", 14, {DIM, N_FF}) &&
+                   need(p + "ffn_down.weight", 14, {N_FF, DIM})
+             : need(p + "ffn_gate_inp.weight", 0, {DIM, N_EXPERT}) && need(p + "exp_probs_b.bias", 0, {N_EXPERT}) &&
+                   need(p + "ffn_gate_exps.weight", 14, {DIM, EXPERT_FF, N_EXPERT}) &&
+                   need(p + "ffn_up_exps.weight", 14, {DIM, EXPERT_FF, N_EXPERT}) &&
+                   need(p + "ffn_down_exps.weight", 14, {EXPERT_FF, DIM, N_EXPERT});
+    if (!ok) return false;
+  }
+  return true;
+}
+
+bool EngineImpl::load(const char* path) {
+  GgufFile f;
+  if (!f.open(path)) {
+    set_err(this, "parse GGUF header: " + f.err());
+    return false;
+  }
+  std::string verr;
+  if (!read_hparams(f, hp, verr) || !check_tensors(f, hp, verr)) {
+    set_err(this, verr);
+    return false;
+  }
+  const uint32_t nl = hp.n_layers, vocab = hp.vocab;
+  std::vector<uint32_t> kvh(hp.kv_heads, hp.kv_heads + nl);
 
   auto need = [&](const std::string& name, uint32_t type, std::vector<uint64_t> ne_) -> const GgufTensor& {
     const GgufTensor* t = f.tensor(name);
@@ -1160,6 +1219,26 @@ lfm_status check_ids(lfm_engine* e, const uint32_t* ids, uint32_t n, int64_t sta
 
 extern "C" {
 
+lfm_status lfm_model_inspect(const char* gguf_path, lfm_hparams* out) {
+  if (!gguf_path) {
+    lfm::g_error = "null argument";
+    return LFM_ERR_ARG;
+  }
+  lfm::GgufFile f;
+  if (!f.open(gguf_path)) {
+    lfm::g_error = "parse GGUF header: " + f.err();
+    return LFM_ERR_MODEL;
+  }
+  lfm_hparams hp;
+  std::string err;
+  if (!lfm::read_hparams(f, hp, err) || !lfm::check_tensors(f, hp, err)) {
+    lfm::g_error = err;
+    return LFM_ERR_MODEL;
+  }
+  if (out) *out = hp;
+  return LFM_OK;
+}
+
 lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out) {
   if (!gguf_path || !out) {
     lfm::g_error = "null argument";
@@ -1369,7 +1448,9 @@ lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint3
         return LFM_ERR_ARG;
       }
     }
+    I.batch.last_count = 0;
     I.run_batch_decode(count, tokens, positions, sessions, next_tokens);
+    I.batch.last_count = count;
     return LFM_OK;
   });
 }
@@ -1377,8 +1458,9 @@ lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint3
 lfm_status lfm_batch_logits(lfm_engine* e, uint32_t index, float* logits) {
   return guarded(e, [&]() -> lfm_status {
     EngineImpl& I = e->impl;
-    if (!logits || I.batch.nsess == 0 || index >= I.batch.nsess) {
-      lfm::set_err(&I, "batch logits: bad arguments");
+    if (!logits || I.batch.nsess == 0 || index >= I.batch.last_count) {
+      lfm::set_err(&I, "batch logits: index " + std::to_string(index) + " is not an entry of the last batch decode step (" +
+                           std::to_string(I.batch.last_count) + " entries)");
       return LFM_ERR_ARG;
     }
     CK(cudaMemcpy(logits, I.batch.logits + (size_t)index * I.hp.vocab, (size_t)I.hp.vocab * 4,

@@ -30,6 +30,32 @@ bool ggml_block_info(uint32_t type, uint64_t& block, uint64_t& bytes) {
 
 namespace {
 
+// Well-formed UTF-8 (RFC 3629): no overlong forms, no surrogates, nothing
+// above U+10FFFF; the check Rust's String::from_utf8 makes.
+bool valid_utf8(const std::string& s) {
+  const unsigned char* p = (const unsigned char*)s.data();
+  size_t i = 0, n = s.size();
+  while (i < n) {
+    unsigned c = p[i];
+    if (c < 0x80) { i++; continue; }
+    int len;
+    unsigned cp;
+    if ((c & 0xE0) == 0xC0) { len = 2; cp = c & 0x1F; }
+    else if ((c & 0xF0) == 0xE0) { len = 3; cp = c & 0x0F; }
+    else if ((c & 0xF8) == 0xF0) { len = 4; cp = c & 0x07; }
+    else return false;
+    if (i + len > n) return false;
+    for (int k = 1; k < len; k++) {
+      if ((p[i + k] & 0xC0) != 0x80) return false;
+      cp = (cp << 6) | (p[i + k] & 0x3F);
+    }
+    if ((len == 2 && cp < 0x80) || (len == 3 && cp < 0x800) || (len == 4 && cp < 0x10000)) return false;
+    if (cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF)) return false;
+    i += len;
+  }
+  return true;
+}
+
 // Buffered sequential reader over the header region.
 class Reader {
  public:
@@ -50,12 +76,23 @@ class Reader {
     return true;
   }
   template <class T> bool get(T& v) { return bytes(&v, sizeof(T)); }
-  bool str(std::string& s) {
+  // GGUF string: u64 length, then UTF-8 bytes (gguf.rs read_string). A
+  // violation other than running out of file leaves its message in `err`.
+  bool str(std::string& s, std::string& err) {
     uint64_t n;
     if (!get(n)) return false;
-    if (n > len_) return false;
+    if (n > (1ull << 30)) {
+      err = "String length " + std::to_string(n) + " exceeds maximum (1 GiB)";
+      return false;
+    }
+    if (n > len_) return false;  // longer than the file: truncated
     s.resize(n);
-    return n == 0 || bytes(&s[0], n);
+    if (n && !bytes(&s[0], n)) return false;
+    if (!valid_utf8(s)) {
+      err = "Invalid UTF-8 in string";
+      return false;
+    }
+    return true;
   }
   uint64_t position() const { return consumed_; }
 
@@ -94,7 +131,7 @@ bool read_value(Reader& r, uint32_t t, GgufValue& v, std::string& err, int depth
       v.u = x;
       return true;
     }
-    case 8: v.kind = GgufValue::STRING; return r.str(v.s);
+    case 8: v.kind = GgufValue::STRING; return r.str(v.s, err);
     case 9: {
       uint32_t et;
       uint64_t n;
@@ -137,14 +174,19 @@ bool GgufFile::open(const std::string& path) {
   if (version != 3) { err_ = "Unsupported GGUF version: " + std::to_string(version) + " (expected 3)"; return false; }
   if (!r.get(tensor_count) || !r.get(kv_count)) { err_ = trunc; return false; }
   const uint64_t MAX_COUNT = 100000;
-  if (tensor_count > MAX_COUNT) { err_ = "Tensor count exceeds maximum"; return false; }
-  if (kv_count > MAX_COUNT) { err_ = "KV count exceeds maximum"; return false; }
+  if (tensor_count > MAX_COUNT) {
+    err_ = "Tensor count " + std::to_string(tensor_count) + " exceeds maximum (100000)";
+    return false;
+  }
+  if (kv_count > MAX_COUNT) {
+    err_ = "KV count " + std::to_string(kv_count) + " exceeds maximum (100000)";
+    return false;
+  }
   for (uint64_t i = 0; i < kv_count; i++) {
-    std::string key;
+    std::string key, e;
     uint32_t vt;
-    if (!r.str(key) || !r.get(vt)) { err_ = trunc; return false; }
+    if (!r.str(key, e) || !r.get(vt)) { err_ = e.empty() ? trunc : e; return false; }
     GgufValue v;
-    std::string e;
     if (!read_value(r, vt, v, e, 0)) { err_ = e.empty() ? trunc : e; return false; }
     if (meta_.count(key)) { err_ = "Duplicate metadata key: " + key; return false; }
     meta_[key] = std::move(v);
@@ -158,7 +200,8 @@ bool GgufFile::open(const std::string& path) {
   for (uint64_t i = 0; i < tensor_count; i++) {
     GgufTensor t;
     uint32_t nd;
-    if (!r.str(t.name) || !r.get(nd)) { err_ = trunc; return false; }
+    std::string e;
+    if (!r.str(t.name, e) || !r.get(nd)) { err_ = e.empty() ? trunc : e; return false; }
     if (nd > 8) { err_ = "Too many dimensions: " + std::to_string(nd) + " (max 8)"; return false; }
     t.ne.resize(nd);
     for (uint32_t d = 0; d < nd; d++)
@@ -176,7 +219,12 @@ bool GgufFile::open(const std::string& path) {
     if (empty) {
       t.nbytes = 0;
     } else {
-      if (block > 1 && n % block != 0) { err_ = "Tensor " + t.name + " elements not a multiple of block size"; return false; }
+      if (block > 1 && n % block != 0) {
+        err_ = "Tensor has " + std::to_string(n) + " elements, not a multiple of block size " +
+               std::to_string(block) + " for GGML type " + std::to_string(t.type);
+        return false;
+      }
+      if (n / block > UINT64_MAX / bpb) { err_ = "Tensor size overflow"; return false; }
       t.nbytes = n / block * bpb;
     }
     if (by_name_.count(t.name)) { err_ = "Duplicate tensor name: " + t.name; return false; }
@@ -185,12 +233,21 @@ bool GgufFile::open(const std::string& path) {
   }
   uint64_t pos = r.position();
   data_offset_ = (pos + alignment_ - 1) / alignment_ * alignment_;
-  if (data_offset_ > file_len_) { err_ = "Data offset exceeds file length"; return false; }
+  if (data_offset_ > file_len_) {
+    err_ = "Data offset " + std::to_string(data_offset_) + " exceeds file length " + std::to_string(file_len_);
+    return false;
+  }
   uint64_t data_size = file_len_ - data_offset_;
   for (auto& t : tensors_) {
-    if (t.offset > data_size) { err_ = "Tensor \"" + t.name + "\" offset exceeds data size"; return false; }
-    if (t.offset + t.nbytes < t.offset || t.offset + t.nbytes > data_size) {
-      err_ = "Tensor \"" + t.name + "\" end exceeds data size";
+    if (t.offset > data_size) {
+      err_ = "Tensor \"" + t.name + "\" offset " + std::to_string(t.offset) + " exceeds data size " +
+             std::to_string(data_size);
+      return false;
+    }
+    if (t.offset + t.nbytes < t.offset) { err_ = "Tensor \"" + t.name + "\" offset+nbytes overflow"; return false; }
+    if (t.offset + t.nbytes > data_size) {
+      err_ = "Tensor \"" + t.name + "\" end " + std::to_string(t.offset + t.nbytes) + " exceeds data size " +
+             std::to_string(data_size);
       return false;
     }
     t.offset += data_offset_;

@@ -358,21 +358,50 @@ static __device__ __align__(256) float2 g_argmax_scratch[kNoAllocPartials + 1];
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 float2* g_scratch_ptr[kMaxDevices] = {};
+void* g_scratch_ctx[kMaxDevices] = {};  // the context each cached address belongs to
+
+// cuCtxGetCurrent through the runtime's driver entry point (no link against
+// libcuda); null if the driver does not offer it.
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (CtxGetCurrentFn)p;
+  });
+  return fn;
+}
 
 // Device address of g_argmax_scratch on the current device. In host code the
 // array's name is only a host-side stand-in, not a device address, so the
-// address is looked up once per device, with that device current, and cached.
+// address is looked up once per device, with that device current, and cached
+// together with the context it was looked up in. A device reset
+// (cudaDeviceReset) replaces the primary context and unloads the module; the
+// next call sees a different context and looks the address up again instead
+// of handing the kernel a stale pointer.
 cudaError_t argmax_scratch(float2** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  auto current_ctx = [] {
+    void* c = nullptr;
+    if (CtxGetCurrentFn f = ctx_get_current_fn())
+      if (f(&c) != 0) c = nullptr;
+    return c;
+  };
+  void* ctx = current_ctx();  // null before the runtime has made a context current
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (!g_scratch_ptr[dev] || !ctx || g_scratch_ctx[dev] != ctx) {
     float2* ptr = nullptr;
     e = cudaGetSymbolAddress((void**)&ptr, g_argmax_scratch);
     if (e != cudaSuccess) return e;
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = current_ctx();  // the lookup made the device's primary context current
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;

@@ -43,7 +43,7 @@ _lib = None
 
 # Every symbol declared in include/lfm_cuda.h.
 EXPORTS = [
-    "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
+    "lfm_model_inspect", "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
     "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
     "lfm_batch_create", "lfm_batch_prefill", "lfm_batch_decode", "lfm_batch_logits",
     "lfm_step_trace", "lfm_engine_info",
@@ -67,6 +67,7 @@ def lib() -> ctypes.CDLL:
     P, U32, I64, SZ = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int64, ctypes.c_size_t
     st = ctypes.c_int32
     sig = {
+        "lfm_model_inspect": ([ctypes.c_char_p, ctypes.POINTER(Hparams)], st),
         "lfm_engine_create": ([ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(P)], st),
         "lfm_engine_destroy": ([P], None),
         "lfm_engine_set_ctx": ([P, U32], st),
@@ -116,6 +117,17 @@ def lib() -> ctypes.CDLL:
 
 def _p(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def model_inspect(gguf_path: str) -> Hparams:
+    """Validate a model file without a device (lfm_model_inspect): the GGUF
+    header rules, the hyperparameters and the tensor table. Raises LfmError
+    with the library's message."""
+    hp = Hparams()
+    st = lib().lfm_model_inspect(gguf_path.encode(), ctypes.byref(hp))
+    if st != 0:
+        raise LfmError(f"lfm_model_inspect: {lib().lfm_global_error().decode()} (status {st})")
+    return hp
 
 
 def ops_check(status: int, what: str):

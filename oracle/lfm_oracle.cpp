@@ -375,6 +375,9 @@ struct Engine {
   std::vector<size_t> kv_ctx;                       // ctx each layer's cache was sized with
   std::string err;
   std::vector<float> last_logits;
+  // session state saved by oracle_checkpoint (test/bench helper, no reference counterpart)
+  std::vector<std::vector<float>> saved_conv, saved_keys, saved_values;
+  std::vector<size_t> saved_kv_ctx;
 
   const TInfo* t(const std::string& n) const {
     auto it = g.by_name.find(n);
@@ -988,6 +991,25 @@ int oracle_greedy(void* h, const uint32_t* prompt, int prompt_len, int n, uint32
     if (step_logits) memcpy(step_logits + (size_t)(step + 1) * e.vocab, logits.data(), (size_t)e.vocab * 4);
   }
   return count;
+}
+
+// Save / put back the session state (K/V caches, conv states): lets a
+// caller re-run the same decode steps, e.g. on a different thread count to
+// check that the results are bit-identical. Not part of the reference.
+void oracle_checkpoint(void* h) {
+  Engine& e = *(Engine*)h;
+  e.saved_conv = e.conv_cache;
+  e.saved_keys = e.keys;
+  e.saved_values = e.values;
+  e.saved_kv_ctx = e.kv_ctx;
+}
+
+void oracle_rollback(void* h) {
+  Engine& e = *(Engine*)h;
+  e.conv_cache = e.saved_conv;
+  e.keys = e.saved_keys;
+  e.values = e.saved_values;
+  e.kv_ctx = e.saved_kv_ctx;
 }
 
 int oracle_num_threads() {

@@ -65,6 +65,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_snapshot.restype = SZ
         L.oracle_greedy.argtypes = [P, P, I32, I32, U32, P, P]
         L.oracle_greedy.restype = I32
+        L.oracle_checkpoint.argtypes = [P]
+        L.oracle_checkpoint.restype = None
+        L.oracle_rollback.argtypes = [P]
+        L.oracle_rollback.restype = None
         L.oracle_num_threads.restype = I32
         L.oracle_set_threads.argtypes = [I32]
         L.oracle_set_threads.restype = None
@@ -156,6 +160,14 @@ class OracleEngine:
         if lib().oracle_forward(self.h, _p(ids), ids.size, start_pos, _p(out)) != 0:
             raise RuntimeError(lib().oracle_engine_error(self.h).decode())
         return out
+
+    def checkpoint(self):
+        """Save the session state (K/V caches, conv states)."""
+        lib().oracle_checkpoint(self.h)
+
+    def rollback(self):
+        """Put back the state saved by checkpoint()."""
+        lib().oracle_rollback(self.h)
 
     def snapshot(self, valid: int) -> np.ndarray:
         n = lib().oracle_snapshot(self.h, valid, None)

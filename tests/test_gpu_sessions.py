@@ -98,3 +98,10 @@ def test_batch_validation(engine):
         engine.batch_decode([0], [1], [256])  # position beyond the context
     with pytest.raises(lfm2_b200.LfmError):
         engine.batch_prefill(5, np.arange(1, 5, dtype=np.uint32))
+    # batch_logits takes only entries of the last batch_decode step
+    with pytest.raises(lfm2_b200.LfmError, match="not an entry"):
+        engine.batch_logits(0)  # no step yet
+    engine.batch_decode([0], [1], [4])
+    assert engine.batch_logits(0).shape == (128000,)
+    with pytest.raises(lfm2_b200.LfmError, match="not an entry"):
+        engine.batch_logits(1)  # a slot, but not an entry of that one-session step
