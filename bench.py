@@ -226,7 +226,7 @@ def microbench(device: int) -> list:
             ids = ids.contiguous()
             x = torch.randn(4 * ind, device="cuda")
             y = torch.empty(4 * outd, device="cuda")
-            xs = ind if ind == 1792 else 0  # down: one input per slot; gate/up: a shared input
+            xs = ind  # one input row per slot (gate/up: the same row four times)
             cycle = copies * 8
 
             def call(i):
@@ -251,7 +251,7 @@ def microbench(device: int) -> list:
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000 / iters
         k = routed or 1
-        alg = k * (q6_bytes(ind, outd) + 4 * outd) + (k if ind == 1792 and routed else 1) * 4 * ind
+        alg = k * (q6_bytes(ind, outd) + 4 * outd + 4 * ind)
         out.append({"shape": name, "us_per_call": round(us, 2), "bytes": int(alg), "gb_s": round(alg / us / 1e3, 1),
                     "frac": round(alg / us / 1e3 / peak, 4)})
         del pool

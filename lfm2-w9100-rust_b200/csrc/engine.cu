@@ -823,6 +823,8 @@ __global__ void k_advance(int* io, uint32_t* rec) {
 
 // `steps` decode steps, each consuming the previous step's argmax, with no host
 // round trip in between; out_tokens receives the argmax of every step.
+// k_advance records each step's INPUT token (the previous step's argmax), so
+// the argmax of step i is record i + 1, and the last step's is io[2].
 void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
   if (steps > loop_cap) {
     if (loop_tokens) cudaFree(loop_tokens);
@@ -850,7 +852,9 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
   CK(cudaEventRecord(ev0, stream));
   for (uint32_t i = 0; i < steps; i++) CK(cudaGraphLaunch(loop_graph, stream));
   CK(cudaEventRecord(ev1, stream));
-  CK(cudaMemcpyAsync(out_tokens, loop_tokens, (size_t)steps * 4, cudaMemcpyDeviceToHost, stream));
+  if (steps > 1)
+    CK(cudaMemcpyAsync(out_tokens, loop_tokens + 1, (size_t)(steps - 1) * 4, cudaMemcpyDeviceToHost, stream));
+  CK(cudaMemcpyAsync(out_tokens + steps - 1, io + 2, 4, cudaMemcpyDeviceToHost, stream));
   CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, stream));
   if (step_active()) CK(cudaMemcpyAsync(h_io + 5, &ctl->err, 4, cudaMemcpyDeviceToHost, stream));
   CK(cudaStreamSynchronize(stream));
