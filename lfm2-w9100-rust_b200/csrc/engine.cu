@@ -113,7 +113,7 @@ struct EngineImpl {
   bool use_mvt = true;  // TMA-staged decode matvecs
   bool use_step = true;  // persistent decode step (LFM_STEP=0 selects the kernel chain)
   bool use_tc = true;    // tensor-core Q6_K prompt GEMMs (LFM_PREFILL=fp32 selects the CUDA-core GEMMs)
-  int tc_min = 16;       // prompts of at least this many tokens use them (LFM_TC_MIN_TOKENS)
+  int tc_min = 1;        // token batches of at least this many tokens use them (LFM_TC_MIN_TOKENS)
   TcScratch tcs;
   std::string step_reason;  // why the persistent step is not in use
   StepCtl* ctl = nullptr;

@@ -5,7 +5,7 @@ The prompt path picks a token tile of 16/32/64/128 tokens per GEMM (the
 smallest holding the prompt, or for the routed experts the average expert's
 share), splits single-tile GEMMs over K, and pads the last tile; attention
 walks 128-position key tiles. Lengths just past each boundary exercise the
-padding and the split. Contract as in the full-model tests (lfm.rs forward,
+padding and the split; prompts of 2-15 tokens run in one padded 16-token tile. Contract as in the full-model tests (lfm.rs forward,
 main.rs:174-195): last-token logits max-abs <= 1e-2 against the oracle, same
 argmax wherever the oracle's top-2 margin exceeds twice the observed error.
 """
@@ -26,7 +26,7 @@ def engine(synth_model, cuda_lib):
     e.close()
 
 
-@pytest.mark.parametrize("n", [17, 33, 65, 129, 200])
+@pytest.mark.parametrize("n", [2, 4, 8, 15, 17, 33, 65, 129, 200])
 def test_prefill_logits_vs_oracle(engine, synth_model, oracle_mod, n):
     p = np.random.default_rng(1000 + n).integers(0, 128000, n).astype(np.uint32)
     o = oracle_mod.OracleEngine(synth_model, kv_f16=True)

@@ -6,10 +6,9 @@ Contract: a session slot behaves like the reference's single session
 snapshot/restore in persistent.rs:164-176). Each session is prefilled with its
 own prompt (the single-session prompt path, so first tokens and states are
 identical), then all sessions advance one token per batched step. The batched
-step computes every matrix as a multi-token GEMM: with fewer than 16 tokens it
-is the fp32 CUDA-core GEMM (logits within 1e-3 of the single-session decode
-kernel), from 16 tokens the tensor-core GEMM with hi/lo activations (within
-1e-2, the parity bar of the full model). Inputs are teacher-forced with the
+step computes every matrix as a multi-token tensor-core GEMM with hi/lo
+activations (one padded 16-token tile below 16 sessions): logits within 1e-2
+of the single-session decode kernel, the parity bar of the full model. Inputs are teacher-forced with the
 single-session tokens so every step compares identical inputs; tokens must
 agree wherever the single-session top-2 margin exceeds twice the tolerance.
 """
@@ -42,7 +41,7 @@ def _single(e, prompt, steps):
     return toks, logits
 
 
-@pytest.mark.parametrize("n_sess,tol", [(5, 1e-3), (20, 1e-2)])
+@pytest.mark.parametrize("n_sess,tol", [(5, 1e-2), (20, 1e-2)])
 def test_batch_matches_single_sessions(engine, n_sess, tol):
     rng = np.random.default_rng(n_sess)
     steps = 6
