@@ -174,6 +174,16 @@ def reduce_max(pg, v: float) -> float:
     return float(t.item())
 
 
+def reduce_sum(pg, v: float) -> float:
+    if pg is None:
+        return v
+    import torch
+    dev = "cpu" if pg.get_backend() == "gloo" else "cuda"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return float(t.item())
+
+
 def prompt(n: int, seed: int) -> np.ndarray:
     return np.random.default_rng(seed).integers(0, VOCAB, n).astype(np.uint32)
 
@@ -402,6 +412,57 @@ def multi_session(eng, peaks, pg, ws: int, info: dict) -> dict:
                          "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4)}}
 
 
+EP_SESSIONS = 8
+
+
+def ep_compare(eng, pg, ws: int, rank: int) -> dict:
+    """Config 4's expert-parallel variant against replicas (N > 1 only):
+    EP_SESSIONS prompts per rank (lengths U[128, 1024], seeded per rank) are
+    prefilled into session slots twice: as replicas (each rank alone, every
+    expert on every GPU) and expert-parallel (rank r computes experts
+    r*32/N .. (r+1)*32/N - 1 for the tokens of all ranks; routed rows cross
+    NVLink through NCCL point-to-point transfers). Replicas: each rank's
+    summed device time, max over ranks; expert-parallel (collective calls):
+    the max over ranks of each call, summed. Aggregate tok/s = all ranks'
+    prompt tokens / that time. The two paths must give the same logits."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(700 + rank)
+    lens = rng.integers(128, 1025, EP_SESSIONS)
+    prompts = [rng.integers(0, VOCAB, int(n)).astype(np.uint32) for n in lens]
+    idt = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        idt.copy_(torch.from_numpy(np.frombuffer(lfm2_b200.ep_unique_id(), dtype=np.uint8).copy()))
+    pg.broadcast(idt, src=0)
+    eng.ep_init(idt.cpu().numpy().tobytes(), rank, ws)
+    eng.batch_create(EP_SESSIONS)
+    # warm-up of both paths
+    eng.batch_prefill(0, prompts[0][:128])
+    eng.ep_prefill(prompts[0][:128], 0)
+    rep_ms, ep_ms, worst, same = 0.0, 0.0, 0.0, True
+    for i, p in enumerate(prompts):
+        barrier(pg)
+        t_rep = eng.batch_prefill(i, p)
+        rep_ms += eng.last_device_ms()  # replicas run on their own: this rank's total
+        ref = eng.snapshot_resident_logits()
+        barrier(pg)
+        t_ep = eng.ep_prefill(p, i)
+        ep_ms += reduce_max(pg, eng.last_device_ms())
+        got = eng.snapshot_resident_logits()
+        worst = max(worst, float(np.abs(got - ref).max()))
+        same = same and t_rep == t_ep
+    rep_ms = reduce_max(pg, rep_ms)
+    worst = reduce_max(pg, worst)
+    same = reduce_max(pg, 0.0 if same else 1.0) == 0.0
+    eng.ep_finalize()
+    tok = reduce_sum(pg, float(lens.sum()))
+    return {"workload": f"config 4 expert-parallel prefill: {EP_SESSIONS} prompts/rank U[128,1024]",
+            "replica_tok_s": round(tok / (rep_ms / 1000.0), 1), "ep_tok_s": round(tok / (ep_ms / 1000.0), 1),
+            "replica_ms": round(rep_ms, 2), "ep_ms": round(ep_ms, 2), "logits_max_abs_diff": worst,
+            "next_tokens_equal": same, "kept": "ep" if ep_ms < rep_ms else "replicas"}
+
+
 def prefill_only(local: int, n: int) -> dict:
     """One warm-up and one timed n-token prefill on GPU `local` (device time
     of the engine's prefill, CUDA events on its stream)."""
@@ -501,6 +562,7 @@ def main():
     ap.add_argument("--no-micro", action="store_true")
     ap.add_argument("--micro-only", action="store_true", help="only the config-1 Q6_K matvec microbench")
     ap.add_argument("--no-sessions", action="store_true", help="skip config 4 (64 independent sessions per GPU)")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel prefill comparison (N > 1)")
     ap.add_argument("--sessions-only", action="store_true", help="only config 4 on this GPU (profiling entry point)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
                     help="only one warm-up and one timed N-token prefill (profiling entry point)")
@@ -628,6 +690,9 @@ def main():
     multi = None
     if not args.no_sessions:
         multi = multi_session(eng, peaks, pg, ws, info)
+    ep = None
+    if ws > 1 and not args.no_ep:
+        ep = ep_compare(eng, pg, ws, rank)
     micro = None
     if rank == 0 and not args.no_micro:
         micro = microbench(local)
@@ -642,7 +707,8 @@ def main():
                 "data": "synthetic seeded random-init Q6_K weights of the exact architecture",
                 "config": workload_config(ws), "decode_path": path_name,
                 "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk.summary(), "prefill": prefill, "multi_session": multi, "microbench": micro, "cpu_baseline": cpu,
+                "clocks": clk.summary(), "prefill": prefill, "multi_session": multi, "expert_parallel_prefill": ep,
+                "microbench": micro, "cpu_baseline": cpu,
                 "tokens_head": toks[:8]}
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -143,6 +143,36 @@ lfm_status lfm_batch_prefill(lfm_engine* e, uint32_t session, const uint32_t* id
  * (forward_token semantics per session, resident_graph.rs:90-101). */
 lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint32_t* tokens,
                             const uint32_t* positions, uint32_t count, uint32_t* next_tokens);
+/* ---- expert-parallel prompt path (one process per GPU) ---------------
+ * New capability (the reference is single-GPU): the routed-expert FFN of
+ * every MoE layer of a prompt runs on the GPU that owns each expert (expert e
+ * on rank e / (32 / world)); routed (token, rank) activation rows go to the
+ * owner and the down rows come back over NCCL point-to-point transfers, then
+ * they are combined in rank order as the reference's combine does
+ * (kernels/resident.rs:101-117). Attention, short conv, dense FFNs and the
+ * lm_head stay on each rank's own tokens. */
+
+/* A fresh NCCL id (128 bytes) that rank 0 creates and shares with the other
+ * ranks (for example through torch.distributed). */
+lfm_status lfm_ep_unique_id(uint8_t* id_out);
+/* Join the expert-parallel group: world divides 32, 0 <= rank < world. Every
+ * rank calls it with the same id. */
+lfm_status lfm_ep_init(lfm_engine* e, const uint8_t* id, int rank, int world);
+#define LFM_EP_OWN_SESSION 0xFFFFFFFFu
+/* Prefill a fresh prompt of n tokens at position 0, expert-parallel: into
+ * session slot `session` (as lfm_batch_prefill) or, with LFM_EP_OWN_SESSION,
+ * into the engine's own session (as reset_session + forward). Collective:
+ * every rank of the group calls it at the same time (any n >= 1 per rank).
+ * next_token = greedy next token of this rank's prompt. */
+lfm_status lfm_ep_prefill(lfm_engine* e, uint32_t session, const uint32_t* ids, uint32_t n, uint32_t* next_token);
+/* The send plan of one MoE layer (host only, no device): slot j = token * 4 +
+ * rank with expert sel[j] goes to rank sel[j] / (32 / world); counts[world] =
+ * slots per destination, order[nslots] = slot of each send position
+ * (destinations ascending, slots ascending within one). */
+lfm_status lfm_ep_plan(const int32_t* sel, uint32_t nslots, uint32_t world, int32_t* counts, int32_t* order);
+/* Leave the expert-parallel group (before the process group is torn down). */
+lfm_status lfm_ep_finalize(lfm_engine* e);
+
 /* Full logits (vocab floats) of entry `index` of the last lfm_batch_decode
  * step (snapshot_resident_logits, resident_graph.rs:561-568, for one batch entry). */
 lfm_status lfm_batch_logits(lfm_engine* e, uint32_t index, float* logits);

@@ -32,6 +32,7 @@
 #include "gguf.h"
 #include "kernels.h"
 #include "step.h"
+#include "ep.h"
 #include "tc_gemm.h"
 
 namespace lfm {
@@ -157,6 +158,17 @@ struct EngineImpl {
   std::string err;
   int launches_per_decode = 0;
 
+  // expert-parallel prompt path (ep.h): communicator and exchange buffers
+  EpComm ep;
+  bool ep_on = false;
+  bool ep_now = false;  // the prompt being run uses the expert-parallel MoE layers
+  int ep_cap_send = 0, ep_cap_recv = 0;  // slots
+  float *ep_send = nullptr, *ep_recv = nullptr, *ep_back = nullptr, *ep_local = nullptr;
+  int32_t *ep_send_tag = nullptr, *ep_recv_tag = nullptr, *ep_order = nullptr, *ep_sel4 = nullptr,
+          *ep_counts = nullptr, *ep_all = nullptr;
+  std::vector<void*> ep_allocs;
+  std::vector<int32_t> h_sel, h_order, h_counts, h_all;
+
   ~EngineImpl() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
@@ -167,6 +179,8 @@ struct EngineImpl {
     free_prefill();
     free_state();
     batch_free();
+    for (void* p : ep_allocs) cudaFree(p);
+    ep_comm_destroy(ep);
     for (void* p : weight_allocs) cudaFree(p);
     if (h_io) cudaFreeHost(h_io);
     if (stream) cudaStreamDestroy(stream);
@@ -220,12 +234,14 @@ struct EngineImpl {
   void enqueue_ffn(const LayerW& L, float* xr, const LaunchCfg& c, unsigned* err);
   void check_device_error();
   void run_decode(uint32_t token, uint32_t pos);
-  void run_prefill(const uint32_t* ids, int n, uint32_t start);
+  void run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep_mode = false);
+  void ep_moe(const LayerW& L, const float* rows, int n, float* xres);
+  void ep_reserve(int send_slots, int recv_slots);
   void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl);
   BatchState batch;
   void batch_create(uint32_t nsess);
   void batch_free();
-  uint32_t batch_prefill(uint32_t sess, const uint32_t* ids, int n);
+  uint32_t batch_prefill(uint32_t sess, const uint32_t* ids, int n, bool ep_mode = false);
   void run_batch_decode(uint32_t count, const uint32_t* tokens, const uint32_t* pos, const uint32_t* sess,
                         uint32_t* next);
   void run_loop(uint32_t steps, uint32_t* out_tokens);
@@ -929,8 +945,15 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
     const bool last = l == hp.n_layers - 1;
     if (last && !tb) {
       // The last layer's FFN only runs on the last token (lfm.rs:540-541).
-      enqueue_ffn(L, px + (size_t)(n - 1) * DIM, c, (unsigned*)(io + 4));
-      nl += L.dense ? 2 : 3;
+      float* xl = px + (size_t)(n - 1) * DIM;
+      if (ep_now && !L.dense) {
+        rmsnorm_n(xl, L.ffn_norm, eps, 1, ph, s);
+        ep_moe(L, ph, 1, xl);
+        nl += 8;
+      } else {
+        enqueue_ffn(L, xl, c, (unsigned*)(io + 4));
+        nl += L.dense ? 2 : 3;
+      }
       continue;
     }
     if (tc && L.dense) CK(tc_split_norm(px, L.ffn_norm, eps, n, ph, tcs, s));
@@ -946,6 +969,9 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
       }
       mm(L.down, psw, px, DIM, true);
       nl += 1;
+    } else if (ep_now && !tb) {
+      ep_moe(L, ph, n, px);
+      nl += 8;
     } else {
       router_logits_n(L.router, ph, n, prlog, s);
       route_n(prlog, L.bias, N_EXPERT, n, psel, pselw, s);
@@ -971,16 +997,127 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
   }
 }
 
-void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start) {
-  ensure_prefill(n);
+// Exchange buffers of the expert-parallel MoE layers (grown, never shrunk).
+void EngineImpl::ep_reserve(int send_slots, int recv_slots) {
+  if (!ep_counts) {
+    ep_counts = dalloc<int32_t>(ep_allocs, 64);
+    ep_all = dalloc<int32_t>(ep_allocs, 64 * 64);
+  }
+  if (send_slots > ep_cap_send) {
+    ep_send = dalloc<float>(ep_allocs, (size_t)send_slots * DIM);
+    ep_back = dalloc<float>(ep_allocs, (size_t)send_slots * DIM);
+    ep_local = dalloc<float>(ep_allocs, (size_t)send_slots * DIM);
+    ep_send_tag = dalloc<int32_t>(ep_allocs, send_slots);
+    ep_order = dalloc<int32_t>(ep_allocs, send_slots);
+    ep_cap_send = send_slots;
+  }
+  if (recv_slots > ep_cap_recv) {
+    ep_recv = dalloc<float>(ep_allocs, (size_t)recv_slots * DIM);
+    CK(cudaMemset(ep_recv, 0, (size_t)recv_slots * DIM * 4));  // padding slots read finite rows
+    ep_recv_tag = dalloc<int32_t>(ep_allocs, recv_slots);
+    ep_sel4 = dalloc<int32_t>(ep_allocs, recv_slots + N_USED);
+    ep_cap_recv = recv_slots;
+  }
+}
+
+// Expert-parallel routed FFN of `n` token rows (`rows`: the FFN inputs after
+// ffn_norm; `xres`: their residual rows): route locally, send each
+// (token, rank) slot's row to the owner of its expert, run this rank's experts
+// on the slots it received (grouped tensor-core GEMMs), send the down rows
+// back and combine them in rank order (kernels/resident.rs:101-117). Every
+// rank of the communicator runs this for the same layer at the same time.
+void EngineImpl::ep_moe(const LayerW& L, const float* rows, int n, float* xres) {
+  cudaStream_t s = stream;
+  const int G = ep.world, me = ep.rank, per = N_EXPERT / G;
+  const int nslots = N_USED * n;
+  std::string e;
+  router_logits_n(L.router, rows, n, prlog, s);
+  route_n(prlog, L.bias, N_EXPERT, n, psel, pselw, s);
+  // send plan on the host (ep_plan), from the routing read back
+  h_sel.resize(nslots);
+  CK(cudaMemcpyAsync(h_sel.data(), psel, (size_t)nslots * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  h_order.resize(nslots);
+  h_counts.assign(G, 0);
+  ep_plan(h_sel.data(), nslots, G, h_counts.data(), h_order.data());
+  CK(cudaMemcpyAsync(ep_order, h_order.data(), (size_t)nslots * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(ep_counts, h_counts.data(), (size_t)G * 4, cudaMemcpyHostToDevice, s));
+  ep_pack(rows, psel, ep_order, nslots, ep_send, ep_send_tag, s);
+  if (!ep_allgather_i32(ep, ep_counts, ep_all, G, s, e)) throw std::runtime_error(e);
+  h_all.resize((size_t)G * G);
+  CK(cudaMemcpyAsync(h_all.data(), ep_all, (size_t)G * G * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  std::vector<int> scnt(G), soff(G), rcnt(G), roff(G);
+  int st = 0, rt = 0;
+  for (int p = 0; p < G; p++) {
+    scnt[p] = h_counts[p];
+    soff[p] = st;
+    st += scnt[p];
+    rcnt[p] = h_all[(size_t)p * G + me];  // rank p's count for this rank
+    roff[p] = rt;
+    rt += rcnt[p];
+  }
+  if (rt + N_USED > ep_cap_recv) throw std::runtime_error("expert-parallel receive buffer too small");
+  if (!ep_exchange(ep, ep_send, ep_send_tag, scnt.data(), soff.data(), ep_recv, ep_recv_tag, rcnt.data(),
+                   roff.data(), DIM, s, e))
+    throw std::runtime_error(e);
+  if (rt > 0) {
+    // the received slots as routing rows of 4 ranks (padding slots: a local
+    // expert over zero rows), then the grouped gate/up -> SwiGLU -> down
+    const int nf = (rt + N_USED - 1) / N_USED;
+    ep_fake_sel(ep_recv_tag, rt, me * per, ep_sel4, s);
+    expert_groups(ep_sel4, nf, pgroups, nf, s);
+    CK(tc_group(pgroups, nf, nf, tcs, s));
+    CK(tc_split_grouped(ep_recv, DIM, 1, nf, tcs, s));
+    CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, nf, pgate, tcs, s));
+    CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, nf, pup, tcs, s));
+    CK(tc_split_grouped(pgate, EXPERT_FF, 1, nf, tcs, s, pup));  // SwiGLU fused into the operand split
+    CK(tc_gemm_q6_grouped(L.down_x, DIM, nf, pdown, tcs, s));
+    ctr.expert_grouped_launches += 3;
+  }
+  // down rows back to the ranks that sent the slots, in the order they came
+  if (!ep_exchange(ep, pdown, nullptr, rcnt.data(), roff.data(), ep_back, nullptr, scnt.data(), soff.data(), DIM, s,
+                   e))
+    throw std::runtime_error(e);
+  ep_unpack(ep_back, ep_order, nslots, ep_local, s);
+  combine_n(ep_local, pselw, n, xres, s);
+}
+
+void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep_mode) {
   cudaStream_t s = stream;
   const float eps = hp.eps;
   int nl = 0;
+  if (ep_mode) {
+    // every rank learns every rank's token count: a rank may receive up to
+    // 4 slots of each of them in one MoE layer
+    ep_reserve(0, 0);
+    h_counts.assign(ep.world, 0);
+    int32_t mine = n;
+    CK(cudaMemcpyAsync(ep_counts, &mine, 4, cudaMemcpyHostToDevice, s));
+    std::string e;
+    if (!ep_allgather_i32(ep, ep_counts, ep_all, 1, s, e)) throw std::runtime_error(e);
+    h_all.assign(ep.world, 0);
+    CK(cudaMemcpyAsync(h_all.data(), ep_all, (size_t)ep.world * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    int total = 0;
+    for (int v : h_all) total += v;
+    ensure_prefill(std::max(n, total));
+    ep_reserve(N_USED * n, N_USED * total + N_USED);
+  } else {
+    ensure_prefill(n);
+  }
+  ep_now = ep_mode;
   CK(cudaEventRecord(ev0, s));
   CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
   embed_n(embd, pids, n, px, s);
   nl++;
-  enqueue_layers(n, start, nullptr, nl);
+  try {
+    enqueue_layers(n, start, nullptr, nl);
+  } catch (...) {
+    ep_now = false;
+    throw;
+  }
+  ep_now = false;
   LaunchCfg c;
   c.stream = s;
   c.pdl = false;
@@ -1036,7 +1173,7 @@ void EngineImpl::batch_free() {
 
 // Prefill session `sess` with its prompt (positions 0..n-1): the single-session
 // prompt path with the session's caches in place of the engine's own.
-uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n) {
+uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n, bool ep_mode) {
   BatchState& B = batch;
   __half* k0 = kc;
   __half* v0 = vc;
@@ -1046,7 +1183,7 @@ uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n) {
   conv_state = B.conv + (size_t)sess * B.conv_stride;
   CK(cudaMemsetAsync(conv_state, 0, B.conv_stride * 4, stream));  // a fresh session (reset_session)
   try {
-    run_prefill(ids, n, 0);
+    run_prefill(ids, n, 0, ep_mode);
   } catch (...) {
     kc = k0, vc = v0, conv_state = c0;
     throw;
@@ -1424,6 +1561,93 @@ lfm_status lfm_batch_prefill(lfm_engine* e, uint32_t session, const uint32_t* id
     if (st) return st;
     const uint32_t t = I.batch_prefill(session, ids, (int)n);
     if (next_token) *next_token = t;
+    return LFM_OK;
+  });
+}
+
+// ---------------------------------------------------------- expert parallel
+lfm_status lfm_ep_unique_id(uint8_t* out) {
+  if (!out) {
+    lfm::g_error = "null argument";
+    return LFM_ERR_ARG;
+  }
+  std::string err;
+  if (!lfm::ep_unique_id(out, err)) {
+    lfm::g_error = err;
+    return LFM_ERR_STATE;
+  }
+  return LFM_OK;
+}
+
+lfm_status lfm_ep_init(lfm_engine* e, const uint8_t* id, int rank, int world) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!id || world < 2 || world > (int)lfm::N_EXPERT || lfm::N_EXPERT % world != 0 || rank < 0 || rank >= world) {
+      lfm::set_err(&I, "expert-parallel group: world must divide 32 (2..32) and 0 <= rank < world");
+      return LFM_ERR_ARG;
+    }
+    if (!I.use_tc) {
+      lfm::set_err(&I, "the expert-parallel prompt path runs on the tensor-core GEMMs (unset LFM_PREFILL=fp32)");
+      return LFM_ERR_STATE;
+    }
+    lfm::ep_comm_destroy(I.ep);
+    I.ep_on = false;
+    std::string err;
+    if (!lfm::ep_comm_init(I.ep, id, rank, world, err)) {
+      lfm::set_err(&I, err);
+      return LFM_ERR_STATE;
+    }
+    I.ep_on = true;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_ep_prefill(lfm_engine* e, uint32_t session, const uint32_t* ids, uint32_t n, uint32_t* next_token) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (!I.ep_on) {
+      lfm::set_err(&I, "no expert-parallel group (lfm_ep_init)");
+      return LFM_ERR_STATE;
+    }
+    lfm_status st = check_ids(e, ids, n, 0);
+    if (st) return st;
+    uint32_t t;
+    if (session == LFM_EP_OWN_SESSION) {
+      I.ensure_state();
+      CK(cudaMemsetAsync(I.conv_state, 0, (size_t)std::max(I.n_conv, 1) * lfm::DIM * 2 * 4, I.stream));
+      I.run_prefill(ids, (int)n, 0, true);
+      t = (uint32_t)I.h_io[2];
+    } else {
+      if (I.batch.nsess == 0 || I.batch.ctx != I.ctx || session >= I.batch.nsess) {
+        lfm::set_err(&I, "session out of range (lfm_batch_create)");
+        return LFM_ERR_ARG;
+      }
+      t = I.batch_prefill(session, ids, (int)n, true);
+    }
+    if (next_token) *next_token = t;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_ep_plan(const int32_t* sel, uint32_t nslots, uint32_t world, int32_t* counts, int32_t* order) {
+  if ((!sel && nslots) || !counts || (!order && nslots) || world < 1 || world > lfm::N_EXPERT ||
+      lfm::N_EXPERT % world != 0) {
+    lfm::g_error = "lfm_ep_plan: bad argument";
+    return LFM_ERR_ARG;
+  }
+  for (uint32_t j = 0; j < nslots; j++)
+    if (sel[j] < 0 || sel[j] >= (int32_t)lfm::N_EXPERT) {
+      lfm::g_error = "lfm_ep_plan: expert id out of range";
+      return LFM_ERR_ARG;
+    }
+  lfm::ep_plan(sel, (int)nslots, (int)world, counts, order);
+  return LFM_OK;
+}
+
+lfm_status lfm_ep_finalize(lfm_engine* e) {
+  return guarded(e, [&]() -> lfm_status {
+    lfm::ep_comm_destroy(e->impl.ep);
+    e->impl.ep_on = false;
     return LFM_OK;
   });
 }

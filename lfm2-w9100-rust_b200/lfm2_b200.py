@@ -46,6 +46,7 @@ EXPORTS = [
     "lfm_model_inspect", "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
     "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
     "lfm_batch_create", "lfm_batch_prefill", "lfm_batch_decode", "lfm_batch_logits",
+    "lfm_ep_unique_id", "lfm_ep_init", "lfm_ep_prefill", "lfm_ep_plan", "lfm_ep_finalize",
     "lfm_step_trace", "lfm_engine_info",
     "lfm_reset_session",
     "lfm_snapshot_cache", "lfm_restore_cache", "lfm_snapshot_logits", "lfm_counters_get",
@@ -81,6 +82,11 @@ def lib() -> ctypes.CDLL:
         "lfm_batch_prefill": ([P, U32, P, U32, ctypes.POINTER(U32)], st),
         "lfm_batch_decode": ([P, P, P, P, U32, P], st),
         "lfm_batch_logits": ([P, U32, P], st),
+        "lfm_ep_unique_id": ([P], st),
+        "lfm_ep_init": ([P, P, ctypes.c_int, ctypes.c_int], st),
+        "lfm_ep_prefill": ([P, U32, P, U32, ctypes.POINTER(U32)], st),
+        "lfm_ep_plan": ([P, U32, U32, P, P], st),
+        "lfm_ep_finalize": ([P], st),
         "lfm_step_trace": ([P, ctypes.c_int, P, SZ, ctypes.POINTER(U32), ctypes.POINTER(U32)], st),
         "lfm_engine_info": ([P], ctypes.c_char_p),
         "lfm_reset_session": ([P], st),
@@ -117,6 +123,27 @@ def lib() -> ctypes.CDLL:
 
 def _p(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def ep_unique_id() -> bytes:
+    """A fresh NCCL id for lfm_ep_init (rank 0 creates it, every rank uses it)."""
+    buf = np.zeros(128, dtype=np.uint8)
+    st = lib().lfm_ep_unique_id(_p(buf))
+    if st != 0:
+        raise LfmError(f"lfm_ep_unique_id: {lib().lfm_global_error().decode()} (status {st})")
+    return buf.tobytes()
+
+
+def ep_plan(sel, world: int):
+    """The expert-parallel send plan of one MoE layer (lfm_ep_plan, host only):
+    (counts per destination rank, send order of the (token, rank) slots)."""
+    sel = np.ascontiguousarray(sel, dtype=np.int32).ravel()
+    counts = np.zeros(world, dtype=np.int32)
+    order = np.zeros(max(sel.size, 1), dtype=np.int32)
+    st = lib().lfm_ep_plan(_p(sel), sel.size, world, _p(counts), _p(order))
+    if st != 0:
+        raise LfmError(f"lfm_ep_plan: {lib().lfm_global_error().decode()} (status {st})")
+    return counts, order[: sel.size]
 
 
 def model_inspect(gguf_path: str) -> Hparams:
@@ -247,6 +274,21 @@ class GpuEngine:
         """Decode path and launch facts of this engine (JSON from the library)."""
         import json
         return json.loads(lib().lfm_engine_info(self.h).decode())
+
+    # -------- expert-parallel prompt path (lfm_ep_*), one process per GPU
+    def ep_init(self, nccl_id: bytes, rank: int, world: int):
+        buf = np.frombuffer(nccl_id, dtype=np.uint8).copy()
+        self._check(lib().lfm_ep_init(self.h, _p(buf), rank, world), "ep_init")
+
+    def ep_prefill(self, ids, session: int = 0xFFFFFFFF) -> int:
+        """Collective: every rank of the group prefills its own prompt."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        t = ctypes.c_uint32()
+        self._check(lib().lfm_ep_prefill(self.h, session, _p(ids), len(ids), ctypes.byref(t)), "ep_prefill")
+        return int(t.value)
+
+    def ep_finalize(self):
+        self._check(lib().lfm_ep_finalize(self.h), "ep_finalize")
 
     def reset_session(self):
         self._check(lib().lfm_reset_session(self.h), "reset_session")

@@ -16,6 +16,7 @@ pub const LFM_ERR_STATE: lfm_status = 4;
 pub const LFM_ERR_DEVICE: lfm_status = 5;
 pub const LFM_MAX_CTX: u32 = 4096;
 pub const LFM_PREFILL_CHUNK: u32 = 64;
+pub const LFM_EP_OWN_SESSION: u32 = 0xFFFF_FFFF;
 
 /// Opaque engine handle.
 #[repr(C)]
@@ -79,6 +80,13 @@ extern "C" {
     pub fn lfm_batch_decode(e: *mut lfm_engine, sessions: *const u32, tokens: *const u32, positions: *const u32,
                             count: u32, next_tokens: *mut u32) -> lfm_status;
     pub fn lfm_batch_logits(e: *mut lfm_engine, index: u32, logits: *mut f32) -> lfm_status;
+    // ---- expert-parallel prompt path (one process per GPU)
+    pub fn lfm_ep_unique_id(id_out: *mut u8) -> lfm_status;
+    pub fn lfm_ep_init(e: *mut lfm_engine, id: *const u8, rank: c_int, world: c_int) -> lfm_status;
+    pub fn lfm_ep_prefill(e: *mut lfm_engine, session: u32, ids: *const u32, n: u32, next_token: *mut u32)
+        -> lfm_status;
+    pub fn lfm_ep_plan(sel: *const i32, nslots: u32, world: u32, counts: *mut i32, order: *mut i32) -> lfm_status;
+    pub fn lfm_ep_finalize(e: *mut lfm_engine) -> lfm_status;
     // ---- diagnostics
     pub fn lfm_step_trace(e: *mut lfm_engine, enable: c_int, out: *mut u64, cap: usize, n_stages: *mut u32,
                           n_ctas: *mut u32) -> lfm_status;
