@@ -156,7 +156,8 @@ lfm_status lfm_batch_decode(lfm_engine* e, const uint32_t* sessions, const uint3
  * ranks (for example through torch.distributed). */
 lfm_status lfm_ep_unique_id(uint8_t* id_out);
 /* Join the expert-parallel group: world divides 32, 0 <= rank < world. Every
- * rank calls it with the same id. */
+ * rank calls it with the same id. A group of one runs the same exchange
+ * through NCCL with itself (all 32 experts local). */
 lfm_status lfm_ep_init(lfm_engine* e, const uint8_t* id, int rank, int world);
 #define LFM_EP_OWN_SESSION 0xFFFFFFFFu
 /* Prefill a fresh prompt of n tokens at position 0, expert-parallel: into

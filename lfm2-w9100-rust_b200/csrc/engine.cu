@@ -163,6 +163,7 @@ struct EngineImpl {
   bool ep_on = false;
   bool ep_now = false;  // the prompt being run uses the expert-parallel MoE layers
   int ep_cap_send = 0, ep_cap_recv = 0;  // slots
+  int ep_total = 0;  // tokens of all ranks in the current expert-parallel prompt
   float *ep_send = nullptr, *ep_recv = nullptr, *ep_back = nullptr, *ep_local = nullptr;
   int32_t *ep_send_tag = nullptr, *ep_recv_tag = nullptr, *ep_order = nullptr, *ep_sel4 = nullptr,
           *ep_counts = nullptr, *ep_all = nullptr;
@@ -1013,7 +1014,7 @@ void EngineImpl::ep_reserve(int send_slots, int recv_slots) {
   }
   if (recv_slots > ep_cap_recv) {
     ep_recv = dalloc<float>(ep_allocs, (size_t)recv_slots * DIM);
-    CK(cudaMemset(ep_recv, 0, (size_t)recv_slots * DIM * 4));  // padding slots read finite rows
+    CK(cudaMemsetAsync(ep_recv, 0, (size_t)recv_slots * DIM * 4, stream));  // padding slots read finite rows
     ep_recv_tag = dalloc<int32_t>(ep_allocs, recv_slots);
     ep_sel4 = dalloc<int32_t>(ep_allocs, recv_slots + N_USED);
     ep_cap_recv = recv_slots;
@@ -1064,10 +1065,16 @@ void EngineImpl::ep_moe(const LayerW& L, const float* rows, int n, float* xres) 
   if (rt > 0) {
     // the received slots as routing rows of 4 ranks (padding slots: a local
     // expert over zero rows), then the grouped gate/up -> SwiGLU -> down
+    // the received slots as nf rows of 4 (padding slots: distinct local
+    // experts over zero-or-stale finite rows). Unlike a real token's four
+    // experts, four received slots may share an expert, so an expert's slot
+    // list can be longer than nf: its capacity is every rank's token count
+    // (one slot per token at most) plus one padding slot.
     const int nf = (rt + N_USED - 1) / N_USED;
+    const int cap = ep_total + 1;
     ep_fake_sel(ep_recv_tag, rt, me * per, ep_sel4, s);
-    expert_groups(ep_sel4, nf, pgroups, nf, s);
-    CK(tc_group(pgroups, nf, nf, tcs, s));
+    expert_groups(ep_sel4, nf, pgroups, cap, s);
+    CK(tc_group(pgroups, cap, nf, tcs, s));
     CK(tc_split_grouped(ep_recv, DIM, 1, nf, tcs, s));
     CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, nf, pgate, tcs, s));
     CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, nf, pup, tcs, s));
@@ -1101,7 +1108,10 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep
     CK(cudaStreamSynchronize(s));
     int total = 0;
     for (int v : h_all) total += v;
-    ensure_prefill(std::max(n, total));
+    // an expert receives at most one slot per token of any rank, plus one
+    // padding slot: its slot list needs total + 1 entries (ep_moe)
+    ep_total = total;
+    ensure_prefill(std::max(n, total + N_USED));
     ep_reserve(N_USED * n, N_USED * total + N_USED);
   } else {
     ensure_prefill(n);
@@ -1582,8 +1592,8 @@ lfm_status lfm_ep_unique_id(uint8_t* out) {
 lfm_status lfm_ep_init(lfm_engine* e, const uint8_t* id, int rank, int world) {
   return guarded(e, [&]() -> lfm_status {
     EngineImpl& I = e->impl;
-    if (!id || world < 2 || world > (int)lfm::N_EXPERT || lfm::N_EXPERT % world != 0 || rank < 0 || rank >= world) {
-      lfm::set_err(&I, "expert-parallel group: world must divide 32 (2..32) and 0 <= rank < world");
+    if (!id || world < 1 || world > (int)lfm::N_EXPERT || lfm::N_EXPERT % world != 0 || rank < 0 || rank >= world) {
+      lfm::set_err(&I, "expert-parallel group: world must divide 32 and 0 <= rank < world");
       return LFM_ERR_ARG;
     }
     if (!I.use_tc) {

@@ -87,7 +87,7 @@ __global__ void k_ep_pack(const float* rows, const int32_t* sel, const int32_t* 
 __global__ void k_ep_fake_sel(const int32_t* tag, int n, int pad, int32_t* sel4) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   const int n4 = (n + N_USED - 1) / N_USED * N_USED;
-  if (j < n4) sel4[j] = j < n ? tag[j] : pad;
+  if (j < n4) sel4[j] = j < n ? tag[j] : pad + (j - n);  // at most 3 padding slots, distinct experts
 }
 
 __global__ void k_ep_unpack(const float* back, const int32_t* order, int n, float* out) {

@@ -42,7 +42,8 @@ bool ep_exchange(const EpComm& c, const float* send, const int32_t* send_tag, co
 void ep_pack(const float* rows, const int32_t* sel, const int32_t* order, int n, float* send, int32_t* tag,
              cudaStream_t s);
 // Received slots as routing rows of 4 ranks for the grouped GEMMs: sel4[j] =
-// tag[j] for j < n, padding slots up to a multiple of 4 take expert `pad`.
+// tag[j] for j < n; the (at most 3) padding slots up to a multiple of 4 take
+// the distinct experts pad, pad + 1, pad + 2 (local experts of this rank).
 void ep_fake_sel(const int32_t* tag, int n, int pad, int32_t* sel4, cudaStream_t s);
 // out[order[i]] = back[i] (rows of DIM floats).
 void ep_unpack(const float* back, const int32_t* order, int n, float* out, cudaStream_t s);

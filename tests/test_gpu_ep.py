@@ -6,7 +6,9 @@ expert-parallel (lfm_ep_prefill: rank r computes experts 16r..16r+15 for the
 tokens of both ranks, routed rows exchanged through NCCL), into session slots
 and into the engine's own session. The routed rows, the expert GEMMs on them
 and the rank-ordered combine are the same arithmetic either way, so logits
-and next tokens must agree (logits within 1e-5; the GEMM tiling may differ).
+and next tokens must agree (logits within 1e-3: the plain path runs the last
+layer's FFN with the decode kernels, the expert-parallel path with the prompt
+GEMMs).
 """
 
 import os
@@ -66,8 +68,34 @@ def test_ep_prefill_matches_single_gpu(synth_model, cuda_lib):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    results = mp.Manager().dict()
+    results = mp.get_context("spawn").Manager().dict()
     mp.spawn(worker, args=(port, synth_model, results), nprocs=2, join=True)
     for rank in (0, 1):
         worst, same = results[rank]
-        assert worst <= 1e-5 and same, (rank, worst, same)
+        assert worst <= 1e-3 and same, (rank, worst, same)
+
+
+def test_ep_group_of_one_matches_local_path(synth_model, cuda_lib):
+    """A group of one GPU runs the whole exchange (plan, pack, NCCL transfers
+    to itself, grouped GEMMs on the received slots, unpack, combine): the
+    result must equal the plain prompt path's."""
+    import lfm2_b200
+    e = lfm2_b200.GpuEngine(synth_model, 0)
+    try:
+        e.set_ctx(512)
+        e.ep_init(lfm2_b200.ep_unique_id(), 0, 1)
+        rng = np.random.default_rng(77)
+        errs = {}
+        for n in (2, 9, 130):
+            p = rng.integers(0, 128000, n).astype(np.uint32)
+            e.reset_session()
+            ref = e.forward(p, 0)
+            t = e.ep_prefill(p)
+            got = e.snapshot_resident_logits()
+            errs[n] = (float(np.abs(got - ref).max()), t == int(np.argmax(ref)))
+        e.ep_finalize()
+        # the plain path runs the last layer's FFN with the decode kernels (f32
+        # activations), the expert-parallel path with the prompt GEMMs (hi/lo)
+        assert all(v[0] <= 1e-3 and v[1] for v in errs.values()), errs
+    finally:
+        e.close()
