@@ -138,6 +138,15 @@ lfm_status lfm_batch_create(lfm_engine* e, uint32_t n_sessions);
  * reset first, like reset_session); *next_token = greedy next token. */
 lfm_status lfm_batch_prefill(lfm_engine* e, uint32_t session, const uint32_t* ids, uint32_t n,
                              uint32_t* next_token);
+/* Fresh prompts of `count` distinct sessions prefilled together (no
+ * reference counterpart: the reference prefills one session at a time):
+ * session sessions[i] gets the lens[i] ids that follow the earlier sessions'
+ * in `ids`, at positions 0..lens[i]-1. Every projection runs as one GEMM over
+ * all the prompts' tokens; attention and the short conv stay per session.
+ * next_tokens[i] = greedy next token of session sessions[i] (as
+ * lfm_batch_prefill). At most 2^20 tokens per call. */
+lfm_status lfm_batch_prefill_many(lfm_engine* e, const uint32_t* sessions, const uint32_t* ids,
+                                  const uint32_t* lens, uint32_t count, uint32_t* next_tokens);
 /* One decode step of `count` distinct sessions: token tokens[i] at position
  * positions[i] of session sessions[i]; next_tokens[i] = greedy next token
  * (forward_token semantics per session, resident_graph.rs:90-101). */

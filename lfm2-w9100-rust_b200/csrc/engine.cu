@@ -97,6 +97,15 @@ struct BatchState {
 
 }  // namespace
 
+// Several sessions' fresh prompts in one pass of the layer stack: session
+// sess[i]'s tokens are rows off[i] .. off[i] + len[i] - 1 (host arrays).
+struct SessRuns {
+  int count = 0;
+  const uint32_t* sess = nullptr;
+  const int* off = nullptr;
+  const int* len = nullptr;
+};
+
 struct EngineImpl {
   int device = 0;
   int sms = 148;
@@ -238,7 +247,9 @@ struct EngineImpl {
   void run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep_mode = false);
   void ep_moe(const LayerW& L, const float* rows, int n, float* xres);
   void ep_reserve(int send_slots, int recv_slots);
-  void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl);
+  void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs = nullptr);
+  void batch_prefill_many(const uint32_t* sess, const uint32_t* ids, const uint32_t* lens, int count,
+                          uint32_t* next);
   BatchState batch;
   void batch_create(uint32_t nsess);
   void batch_free();
@@ -891,7 +902,7 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
 // tb != nullptr: one token from each of n independent sessions (batched
 // decode): positions, sessions and per-session caches come from tb, and every
 // token runs every layer.
-void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl) {
+void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs) {
   cudaStream_t s = stream;
   const float eps = hp.eps;
   LaunchCfg c;
@@ -926,6 +937,18 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
         qk_prep_batch(pqkv, L.q_norm, L.k_norm, rope, n, ctx, eps, tb->kc + loff, tb->vc + loff, tb->pos, tb->sess,
                       tb->kv_stride, s);
         attn_batch(pqkv, tb->kc + loff, tb->vc + loff, n, ctx, pa, tb->pos, tb->sess, tb->kv_stride, tb->part, s);
+      } else if (runs) {
+        // each session's prompt attends to itself only (its own cache)
+        for (int i = 0; i < runs->count; i++) {
+          const int o = runs->off[i], m = runs->len[i];
+          __half* skc = batch.kc + (size_t)runs->sess[i] * batch.kv_stride + loff;
+          __half* svc = batch.vc + (size_t)runs->sess[i] * batch.kv_stride + loff;
+          qk_prep_n(pqkv + (size_t)o * ld, L.q_norm, L.k_norm, rope, 0, m, ctx, eps, skc, svc, s);
+          if (tc) CK(attn_prefill_tc(pqkv + (size_t)o * ld, ld, skc, svc, 0, m, (int)ctx, pa + (size_t)o * DIM, DIM,
+                                     tcs.err, s));
+          else attn_prefill(pqkv + (size_t)o * ld, skc, svc, 0, m, ctx, pa + (size_t)o * DIM, s);
+          nl += 2;
+        }
       } else {
         qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kc + loff, vc + loff, s);
         if (tc) CK(attn_prefill_tc(pqkv, ld, kc + loff, vc + loff, (int)start, n, (int)ctx, pa, DIM, tcs.err, s));
@@ -937,14 +960,25 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
     } else {
       mm(L.in_proj, ph, pbcx, 3 * DIM, false);
       const size_t coff = (size_t)L.conv_idx * DIM * 2;
-      if (tb) conv_batch(pbcx, L.conv_w, tb->conv + coff, tb->conv_stride, tb->sess, n, pgated, s);
-      else conv_prefill(pbcx, L.conv_w, conv_state + coff, n, pgated, s);
+      if (tb) {
+        conv_batch(pbcx, L.conv_w, tb->conv + coff, tb->conv_stride, tb->sess, n, pgated, s);
+      } else if (runs) {
+        for (int i = 0; i < runs->count; i++) {
+          const int o = runs->off[i];
+          conv_prefill(pbcx + (size_t)o * 3 * DIM, L.conv_w,
+                       batch.conv + (size_t)runs->sess[i] * batch.conv_stride + coff, runs->len[i],
+                       pgated + (size_t)o * DIM, s);
+          nl++;
+        }
+      } else {
+        conv_prefill(pbcx, L.conv_w, conv_state + coff, n, pgated, s);
+      }
       if (tc) split(pgated, DIM);
       mm(L.out_proj, pgated, px, DIM, true);
       nl += tb ? 1 : 2;
     }
     const bool last = l == hp.n_layers - 1;
-    if (last && !tb) {
+    if (last && !tb && !runs) {
       // The last layer's FFN only runs on the last token (lfm.rs:540-541).
       float* xl = px + (size_t)(n - 1) * DIM;
       if (ep_now && !L.dense) {
@@ -1200,6 +1234,66 @@ uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n, bo
   }
   kc = k0, vc = v0, conv_state = c0;
   return (uint32_t)h_io[2];
+}
+
+// Fresh prompts of `count` distinct sessions in one pass (every projection is
+// one GEMM over all their tokens, so each weight is read once per pass):
+// session sess[i] gets ids[off_i .. off_i + lens[i]) at positions 0.. (off_i =
+// sum of the earlier lens); attention and the short conv run per session on
+// its own cache and state. The last layer's FFN runs on every token (the
+// single-session path trims it to the last token; the rows it feeds are the
+// same). next[i] = greedy next token of session sess[i].
+void EngineImpl::batch_prefill_many(const uint32_t* sess, const uint32_t* ids, const uint32_t* lens, int count,
+                                   uint32_t* next) {
+  BatchState& B = batch;
+  std::vector<int> off(count), len(count);
+  int n = 0;
+  for (int i = 0; i < count; i++) {
+    off[i] = n;
+    len[i] = (int)lens[i];
+    n += len[i];
+  }
+  ensure_prefill(std::max(n, count));
+  cudaStream_t s = stream;
+  const float eps = hp.eps;
+  int nl = 0;
+  CK(cudaEventRecord(ev0, s));
+  for (int i = 0; i < count; i++)  // fresh sessions (reset_session)
+    CK(cudaMemsetAsync(B.conv + (size_t)sess[i] * B.conv_stride, 0, B.conv_stride * 4, s));
+  CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  embed_n(embd, pids, n, px, s);
+  nl++;
+  SessRuns runs;
+  runs.count = count;
+  runs.sess = sess;
+  runs.off = off.data();
+  runs.len = len.data();
+  enqueue_layers(n, 0, nullptr, nl, &runs);
+  // the last token of each session: final norm, tied lm_head, row argmax
+  for (int i = 0; i < count; i++)
+    CK(cudaMemcpyAsync(ph + (size_t)i * DIM, px + (size_t)(off[i] + len[i] - 1) * DIM, DIM * 4,
+                       cudaMemcpyDeviceToDevice, s));
+  if (use_tc && count >= tc_min) {
+    CK(tc_split_norm(ph, out_norm, eps, count, pa, tcs, s));
+    CK(tc_gemm_q6(embd, count, B.logits, (int)hp.vocab, false, tcs, s));
+  } else {
+    rmsnorm_n(ph, out_norm, eps, count, pa, s);
+    gemm_q6_ld(embd, pa, count, B.logits, (int)hp.vocab, false, s);
+  }
+  argmax_rows(B.logits, count, (int)hp.vocab, B.next, s);
+  nl += 3 + count;
+  B.last_count = 0;  // the logits rows no longer belong to a decode step
+  std::vector<int> h(count);
+  CK(cudaMemcpyAsync(h.data(), B.next, (size_t)count * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(ev1, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaGetLastError());
+  CK(cudaEventElapsedTime(&last_ms, ev0, ev1));
+  for (int i = 0; i < count; i++) next[i] = (uint32_t)h[i];
+  ctr.kernel_launches += nl;
+  ctr.prefill_tokens += n;
+  check_device_error();
 }
 
 // One decode step of `count` sessions: token tokens[i] at position pos[i] of
@@ -1658,6 +1752,46 @@ lfm_status lfm_ep_finalize(lfm_engine* e) {
   return guarded(e, [&]() -> lfm_status {
     lfm::ep_comm_destroy(e->impl.ep);
     e->impl.ep_on = false;
+    return LFM_OK;
+  });
+}
+
+lfm_status lfm_batch_prefill_many(lfm_engine* e, const uint32_t* sessions, const uint32_t* ids,
+                                  const uint32_t* lens, uint32_t count, uint32_t* next_tokens) {
+  return guarded(e, [&]() -> lfm_status {
+    EngineImpl& I = e->impl;
+    if (I.batch.nsess == 0 || I.batch.ctx != I.ctx) {
+      lfm::set_err(&I, "no session slots for the current context length (lfm_batch_create)");
+      return LFM_ERR_ARG;
+    }
+    if (!sessions || !ids || !lens || !next_tokens || count == 0 || count > I.batch.nsess) {
+      lfm::set_err(&I, "batch prefill: bad arguments");
+      return LFM_ERR_ARG;
+    }
+    std::vector<uint8_t> seen(I.batch.nsess, 0);
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < count; i++) {
+      if (sessions[i] >= I.batch.nsess || seen[sessions[i]]) {
+        lfm::set_err(&I, "batch prefill: sessions must be distinct and in range");
+        return LFM_ERR_ARG;
+      }
+      seen[sessions[i]] = 1;
+      if (lens[i] == 0 || lens[i] > I.ctx) {
+        lfm::set_err(&I, "batch prefill: every prompt needs 1..ctx tokens");
+        return LFM_ERR_ARG;
+      }
+      total += lens[i];
+    }
+    if (total > (1u << 20)) {
+      lfm::set_err(&I, "batch prefill: more than 2^20 tokens in one call");
+      return LFM_ERR_ARG;
+    }
+    for (uint64_t i = 0; i < total; i++)
+      if (ids[i] >= I.hp.vocab) {
+        lfm::set_err(&I, "token out of range");
+        return LFM_ERR_ARG;
+      }
+    I.batch_prefill_many(sessions, ids, lens, (int)count, next_tokens);
     return LFM_OK;
   });
 }

@@ -45,7 +45,7 @@ _lib = None
 EXPORTS = [
     "lfm_model_inspect", "lfm_engine_create", "lfm_engine_destroy", "lfm_engine_set_ctx", "lfm_hparams_get",
     "lfm_forward_logits", "lfm_forward_token", "lfm_generate", "lfm_decode_loop", "lfm_last_device_ms",
-    "lfm_batch_create", "lfm_batch_prefill", "lfm_batch_decode", "lfm_batch_logits",
+    "lfm_batch_create", "lfm_batch_prefill", "lfm_batch_prefill_many", "lfm_batch_decode", "lfm_batch_logits",
     "lfm_ep_unique_id", "lfm_ep_init", "lfm_ep_prefill", "lfm_ep_plan", "lfm_ep_finalize",
     "lfm_step_trace", "lfm_engine_info",
     "lfm_reset_session",
@@ -80,6 +80,7 @@ def lib() -> ctypes.CDLL:
         "lfm_last_device_ms": ([P], ctypes.c_float),
         "lfm_batch_create": ([P, U32], st),
         "lfm_batch_prefill": ([P, U32, P, U32, ctypes.POINTER(U32)], st),
+        "lfm_batch_prefill_many": ([P, P, P, P, U32, P], st),
         "lfm_batch_decode": ([P, P, P, P, U32, P], st),
         "lfm_batch_logits": ([P, U32, P], st),
         "lfm_ep_unique_id": ([P], st),
@@ -241,6 +242,16 @@ class GpuEngine:
         t = ctypes.c_uint32()
         self._check(lib().lfm_batch_prefill(self.h, session, _p(ids), len(ids), ctypes.byref(t)), "batch_prefill")
         return int(t.value)
+
+    def batch_prefill_many(self, sessions, prompts) -> np.ndarray:
+        """Fresh prompts of several sessions in one pass; their next tokens."""
+        ss = np.ascontiguousarray(sessions, dtype=np.uint32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), dtype=np.uint32)
+        lens = np.array([len(p) for p in prompts], dtype=np.uint32)
+        out = np.empty(len(ss), dtype=np.uint32)
+        self._check(lib().lfm_batch_prefill_many(self.h, _p(ss), _p(ids), _p(lens), len(ss), _p(out)),
+                    "batch_prefill_many")
+        return out
 
     def batch_decode(self, sessions, tokens, positions) -> np.ndarray:
         """One decode step of distinct sessions; returns their next tokens."""

@@ -77,6 +77,8 @@ extern "C" {
     pub fn lfm_batch_create(e: *mut lfm_engine, n_sessions: u32) -> lfm_status;
     pub fn lfm_batch_prefill(e: *mut lfm_engine, session: u32, ids: *const u32, n: u32, next_token: *mut u32)
         -> lfm_status;
+    pub fn lfm_batch_prefill_many(e: *mut lfm_engine, sessions: *const u32, ids: *const u32, lens: *const u32,
+                                  count: u32, next_tokens: *mut u32) -> lfm_status;
     pub fn lfm_batch_decode(e: *mut lfm_engine, sessions: *const u32, tokens: *const u32, positions: *const u32,
                             count: u32, next_tokens: *mut u32) -> lfm_status;
     pub fn lfm_batch_logits(e: *mut lfm_engine, index: u32, logits: *mut f32) -> lfm_status;

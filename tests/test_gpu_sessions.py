@@ -104,3 +104,28 @@ def test_batch_validation(engine):
     assert engine.batch_logits(0).shape == (128000,)
     with pytest.raises(lfm2_b200.LfmError, match="not an entry"):
         engine.batch_logits(1)  # a slot, but not an entry of that one-session step
+
+
+def test_prefill_many_matches_one_by_one(engine):
+    """lfm_batch_prefill_many (several prompts in one pass) leaves every
+    session in the state the one-by-one prefill leaves it in: same next
+    tokens, and a following batched decode step gives the same logits (the
+    one-by-one path trims the last layer's FFN to the last token and runs it
+    with the decode kernels, hence the 2e-3 bound)."""
+    rng = np.random.default_rng(41)
+    lens = [3, 70, 1, 129, 16]
+    prompts = [rng.integers(0, 128000, n).astype(np.uint32) for n in lens]
+    sess = [4, 0, 2, 1, 3]
+    engine.batch_create(5)
+    one = [engine.batch_prefill(s, p) for s, p in zip(sess, prompts)]
+    pos = [len(p) for p in prompts]
+    n1 = engine.batch_decode(sess, one, pos)
+    l1 = [engine.batch_logits(i) for i in range(5)]
+    engine.batch_create(5)
+    many = engine.batch_prefill_many(sess, prompts)
+    assert list(many) == one
+    n2 = engine.batch_decode(sess, list(many), pos)
+    l2 = [engine.batch_logits(i) for i in range(5)]
+    worst = max(float(np.abs(a - b).max()) for a, b in zip(l1, l2))
+    assert worst <= 2e-3, worst
+    assert list(n1) == list(n2)
