@@ -41,7 +41,7 @@ SEED = 1234
 # DRAM bytes (read + write) of one decode step, taken from an ncu capture of
 # the same workload (not measured by this run); keyed by decode path, with the
 # profile summary that holds the capture.
-TRAFFIC: dict = {"persistent-step": (1442.7e6, "profiles/k_step_decode_config2.md")}
+TRAFFIC: dict = {"persistent-step": (1447.4e6, "profiles/k_step_decode_config2.md")}
 DIM, VOCAB = 2048, 128000
 N_ATTN, N_CONV, N_DENSE, N_MOE = 6, 18, 2, 22
 
@@ -397,12 +397,15 @@ def multi_session(eng, peaks, pg, ws: int, info: dict) -> dict:
     toks = np.array(toks, np.uint32)
     pos = lens.astype(np.uint32).copy()
     dec_ms = 0.0
+    steps = []
     w1 = time.perf_counter()
     for _ in range(SESSION_GEN):
         toks = eng.batch_decode(sess, toks, pos)
         dec_ms += eng.last_device_ms()
+        steps.append(toks)
         pos += 1
     w2 = time.perf_counter()
+    text = text_stream_rate(steps, sess)
     dec_max = reduce_max(pg, dec_ms)
     pf_max = reduce_max(pg, pf_ms)
     wall_dec = reduce_max(pg, w2 - w1)
@@ -417,6 +420,7 @@ def multi_session(eng, peaks, pg, ws: int, info: dict) -> dict:
             "decode_ms_per_step": round(dec_max / SESSION_GEN, 3),
             "prefill_tok_s": round(ws * float(lens.sum()) / (pf_max / 1000.0), 1),
             "e2e_tok_s": round(gen / wall_all, 1), "e2e_decode_tok_s": round(gen / wall_dec, 1),
+            "text_stream": dict(text, vs_decode=round(text["tok_s"] / (gen / (dec_max / 1000.0)), 1)),
             "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
                          "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4)}}
@@ -471,6 +475,29 @@ def ep_compare(eng, pg, ws: int, rank: int) -> dict:
             "replica_tok_s": round(tok / (rep_ms / 1000.0), 1), "ep_tok_s": round(tok / (ep_ms / 1000.0), 1),
             "replica_ms": round(rep_ms, 2), "ep_ms": round(ep_ms, 2), "logits_max_abs_diff": worst,
             "next_tokens_equal": same, "kept": "ep" if ep_ms < rep_ms else "replicas"}
+
+
+def text_stream_rate(steps, sess) -> dict:
+    """The host text path of the batched decode (lfm_text_push: UTF-8
+    assembly + the decoder's space cleanup per session, as the reference's
+    StreamDecoder + DecodedText) over the tokens the batched steps produced,
+    one push per step, timed on one host thread after the GPU work. Pieces of
+    the synthetic vocabulary: the 16 control tokens render empty, the others
+    are their own ASCII text."""
+    import lfm2_b200
+    pieces = [b"" if i < 16 else b" t%06d" % i for i in range(VOCAB)]
+    t = lfm2_b200.TextStreams(pieces, len(sess), clean_spaces=True, replace_invalid=True)
+    n = 0
+    t0 = time.perf_counter()
+    for toks in steps:
+        t.push(sess, toks)
+        n += len(toks)
+    for s_ in sess:
+        t.finish(int(s_))
+    dt = time.perf_counter() - t0
+    t.close()
+    return {"tok_s": round(n / dt, 1), "threads": 1, "tokens": n,
+            "path": "lfm_text_push (UTF-8 assembly + clean_spaces per session)"}
 
 
 def prefill_only(local: int, n: int) -> dict:

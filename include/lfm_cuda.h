@@ -183,6 +183,35 @@ lfm_status lfm_ep_plan(const int32_t* sel, uint32_t nslots, uint32_t world, int3
 /* Leave the expert-parallel group (before the process group is torn down). */
 lfm_status lfm_ep_finalize(lfm_engine* e);
 
+/* ---- streaming text of sessions decoded together (host only) ---------
+ * The text path that runs beside the GPU loop: per session, token pieces
+ * (raw bytes, possibly ending inside a UTF-8 sequence) are assembled as the
+ * reference's StreamDecoder / Utf8Stream does (tokenizer/src/stream.rs:48-189:
+ * complete text emitted, an incomplete tail kept, invalid bytes an error or
+ * one U+FFFD per maximal invalid subsequence) and cleaned as its DecodedText
+ * does (engine/src/text_output.rs:9-106: the decoder's clean_spaces over the
+ * text so far, the last 16 bytes withheld until more text or the end). The
+ * pieces are the caller's: the tokenizer's token_to_piece(id, render_special)
+ * of every id, concatenated, with piece t at bytes [off[t], off[t+1]). */
+typedef struct lfm_text lfm_text;
+lfm_status lfm_text_create(const uint8_t* piece_bytes, const uint64_t* piece_off, uint32_t n_tokens,
+                           uint32_t n_sessions, int clean_spaces, int replace_invalid, lfm_text** out);
+void lfm_text_destroy(lfm_text* t);
+/* One token for each of `count` entries (sessions may repeat; entries are
+ * applied in order). The text each entry completes is appended to `out`
+ * (capacity `cap` bytes): entry i's text is out[out_off[i], out_off[i+1]).
+ * LFM_ERR_STATE if a session's bytes can never become valid UTF-8 under the
+ * error policy (that session keeps its buffer; call lfm_text_reset). */
+lfm_status lfm_text_push(lfm_text* t, const uint32_t* sessions, const uint32_t* tokens, uint32_t count, char* out,
+                         size_t cap, uint64_t* out_off);
+/* End of a session's stream: its remaining text (withheld suffix, and the
+ * incomplete tail as U+FFFD under the replace policy); the session is empty
+ * afterwards. LFM_ERR_STATE for an incomplete or invalid tail under the
+ * error policy. */
+lfm_status lfm_text_finish(lfm_text* t, uint32_t session, char* out, size_t cap, size_t* len);
+lfm_status lfm_text_reset(lfm_text* t, uint32_t session);
+const char* lfm_text_error(void);
+
 /* Full logits (vocab floats) of entry `index` of the last lfm_batch_decode
  * step (snapshot_resident_logits, resident_graph.rs:561-568, for one batch entry). */
 lfm_status lfm_batch_logits(lfm_engine* e, uint32_t index, float* logits);

@@ -105,6 +105,14 @@ lfm_status lfm_q6k_matmul(const void* w_dev, uint32_t in_dim, uint32_t rows, con
     lfm::LaunchCfg c;
     c.stream = (cudaStream_t)stream;
     lfm::mv_plain(W, lfm::XSrc{x_dev, nullptr, 0.f}, y_dev, c);
+  } else if (n == 1 && in_dim == (uint32_t)lfm::N_FF) {
+    // the decode kernel of the dense down projection (7168-wide rows), which
+    // adds to its output: y = 0 + W x, the same values as a plain store
+    lfm::LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(y_dev, 0, (size_t)rows * 4, c.stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    lfm::mv_down7168_resid(W, x_dev, y_dev, c);
   } else {
     lfm::gemm_q6(W, x_dev, (int)n, y_dev, false, (cudaStream_t)stream);
   }

@@ -54,6 +54,7 @@ EXPORTS = [
     "lfm_q6k_upload", "lfm_q6k_dequant", "lfm_q6k_matmul", "lfm_q6k_routed", "lfm_route",
     "lfm_argmax", "lfm_argmax_noalloc", "lfm_tc_gemm_f16", "lfm_tc_gemm_f16_bmn", "lfm_attention_prefill", "lfm_selftest_wait_timeout", "lfm_q6k_prompt_gemm", "lfm_q6k_prompt_grouped",
     "lfm_ops_error",
+    "lfm_text_create", "lfm_text_destroy", "lfm_text_push", "lfm_text_finish", "lfm_text_reset", "lfm_text_error",
 ]
 
 
@@ -113,6 +114,12 @@ def lib() -> ctypes.CDLL:
         "lfm_q6k_prompt_gemm": ([P, U32, U32, P, U32, P, P], st),
         "lfm_q6k_prompt_grouped": ([P, U32, U32, U32, P, P, U32, U32, P, P], st),
         "lfm_ops_error": ([], ctypes.c_char_p),
+        "lfm_text_create": ([P, P, U32, U32, ctypes.c_int, ctypes.c_int, ctypes.POINTER(P)], st),
+        "lfm_text_destroy": ([P], None),
+        "lfm_text_push": ([P, P, P, U32, P, SZ, P], st),
+        "lfm_text_finish": ([P, U32, P, SZ, ctypes.POINTER(SZ)], st),
+        "lfm_text_reset": ([P, U32], st),
+        "lfm_text_error": ([], ctypes.c_char_p),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -324,3 +331,59 @@ class GpuEngine:
         c = Counters()
         lib().lfm_counters_get(self.h, ctypes.byref(c))
         return {k: int(getattr(c, k)) for k, _ in Counters._fields_}
+
+
+class TextStreams:
+    """Streaming text of many sessions (lfm_text_*): token pieces assembled
+    into UTF-8 text and cleaned as the reference's StreamDecoder + DecodedText
+    do. `pieces[t]` = bytes of token t (the tokenizer's token_to_piece)."""
+
+    def __init__(self, pieces, n_sessions: int, clean_spaces: bool = True, replace_invalid: bool = False):
+        blob = b"".join(pieces)
+        off = np.zeros(len(pieces) + 1, dtype=np.uint64)
+        off[1:] = np.cumsum([len(p) for p in pieces])
+        self._blob = np.frombuffer(blob, dtype=np.uint8).copy() if blob else np.zeros(1, np.uint8)
+        self._off = off
+        h = ctypes.c_void_p()
+        st = lib().lfm_text_create(_p(self._blob), _p(self._off), len(pieces), n_sessions, int(clean_spaces),
+                                   int(replace_invalid), ctypes.byref(h))
+        if st != 0:
+            raise LfmError(f"lfm_text_create: {lib().lfm_text_error().decode()} (status {st})")
+        self.h = h
+        self._cap = 1 << 16
+        self._buf = ctypes.create_string_buffer(self._cap)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lfm_text_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def push(self, sessions, tokens):
+        """One token per entry; returns the bytes each entry completed."""
+        ss = np.ascontiguousarray(sessions, dtype=np.uint32)
+        tt = np.ascontiguousarray(tokens, dtype=np.uint32)
+        off = np.zeros(len(ss) + 1, dtype=np.uint64)
+        st = lib().lfm_text_push(self.h, _p(ss), _p(tt), len(ss), self._buf, self._cap, _p(off))
+        if st != 0:
+            raise LfmError(f"lfm_text_push: {lib().lfm_text_error().decode()} (status {st})")
+        raw = self._buf.raw
+        return [raw[int(off[i]):int(off[i + 1])] for i in range(len(ss))]
+
+    def finish(self, session: int) -> bytes:
+        n = ctypes.c_size_t()
+        st = lib().lfm_text_finish(self.h, session, self._buf, self._cap, ctypes.byref(n))
+        if st != 0:
+            raise LfmError(f"lfm_text_finish: {lib().lfm_text_error().decode()} (status {st})")
+        return self._buf.raw[: n.value]
+
+    def reset(self, session: int):
+        st = lib().lfm_text_reset(self.h, session)
+        if st != 0:
+            raise LfmError(f"lfm_text_reset: {lib().lfm_text_error().decode()} (status {st})")
+

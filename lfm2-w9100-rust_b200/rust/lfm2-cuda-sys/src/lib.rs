@@ -24,6 +24,12 @@ pub struct lfm_engine {
     _p: [u8; 0],
 }
 
+/// Opaque streaming-text handle.
+#[repr(C)]
+pub struct lfm_text {
+    _p: [u8; 0],
+}
+
 /// `lfm_hparams` (engine/src/lfm.rs:31-49).
 #[repr(C)]
 #[derive(Clone, Copy)]
@@ -130,4 +136,14 @@ extern "C" {
                                   y_dev: *mut f32, stream: *mut c_void) -> lfm_status;
     pub fn lfm_selftest_wait_timeout(status: *mut u32, cycles: *mut u64) -> lfm_status;
     pub fn lfm_ops_error() -> *const c_char;
+    // ---- streaming text of sessions decoded together (host only)
+    pub fn lfm_text_create(piece_bytes: *const u8, piece_off: *const u64, n_tokens: u32, n_sessions: u32,
+                           clean_spaces: c_int, replace_invalid: c_int, out: *mut *mut lfm_text) -> lfm_status;
+    pub fn lfm_text_destroy(t: *mut lfm_text);
+    pub fn lfm_text_push(t: *mut lfm_text, sessions: *const u32, tokens: *const u32, count: u32, out: *mut c_char,
+                         cap: usize, out_off: *mut u64) -> lfm_status;
+    pub fn lfm_text_finish(t: *mut lfm_text, session: u32, out: *mut c_char, cap: usize, len: *mut usize)
+        -> lfm_status;
+    pub fn lfm_text_reset(t: *mut lfm_text, session: u32) -> lfm_status;
+    pub fn lfm_text_error() -> *const c_char;
 }
