@@ -26,6 +26,7 @@
 #include <memory>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/lfm_cuda.h"
@@ -123,6 +124,13 @@ struct EngineImpl {
   bool use_mvt = true;  // TMA-staged decode matvecs
   bool use_step = true;  // persistent decode step (LFM_STEP=0 selects the kernel chain)
   bool use_tc = true;    // tensor-core Q6_K prompt GEMMs (LFM_PREFILL=fp32 selects the CUDA-core GEMMs)
+  // prompt GEMMs read load-time expanded fp16 weights (LFM_PREFILL_X16=0: dequantise on chip)
+  bool use_x16 = true;
+  std::unordered_map<const void*, const __half*> x16_of;  // Q6Mat::q -> its fp16 A operand
+  const __half* x16(const Q6Mat& W) const {
+    auto it = x16_of.find(W.q);
+    return it == x16_of.end() ? nullptr : it->second;
+  }
   int tc_min = 1;        // token batches of at least this many tokens use them (LFM_TC_MIN_TOKENS)
   TcScratch tcs;
   std::string step_reason;  // why the persistent step is not in use
@@ -189,6 +197,7 @@ struct EngineImpl {
     free_prefill();
     free_state();
     batch_free();
+    for (auto& kv : x16_of) cudaFree((void*)kv.second);
     for (void* p : ep_allocs) cudaFree(p);
     ep_comm_destroy(ep);
     for (void* p : weight_allocs) cudaFree(p);
@@ -295,6 +304,21 @@ void EngineImpl::upload_q6(const GgufFile& f, const GgufTensor& t, int rows, int
   CK(cudaMemcpy(d, dst.data(), bytes, cudaMemcpyHostToDevice));
   weight_bytes += bytes;
   out = q6_view(d, rows, nb);
+  if (use_x16 && use_tc) {
+    // the prompt GEMMs' fp16 A operand of this matrix (2 bytes per weight);
+    // without room for it the prompt GEMMs dequantise on chip instead
+    void* x = nullptr;
+    if (cudaMalloc(&x, (size_t)rows * nb * QK * 2) != cudaSuccess) {
+      cudaGetLastError();
+      use_x16 = false;
+      for (auto& kv : x16_of) cudaFree((void*)kv.second);
+      x16_of.clear();
+      return;
+    }
+    CK(q6_expand_f16(out, (__half*)x, stream));
+    CK(cudaStreamSynchronize(stream));
+    x16_of[out.q] = (const __half*)x;
+  }
 }
 
 const float* EngineImpl::upload_f32(const GgufFile& f, const GgufTensor& t) {
@@ -918,7 +942,7 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
   };
   // out[t * ldo + o] (+)= W x_t
   auto mm = [&](const Q6Mat& W, const float* X, float* out, int ldo, bool resid) {
-    if (tc) CK(tc_gemm_q6(W, n, out, ldo, resid, tcs, s));
+    if (tc) CK(tc_gemm_q6(W, n, out, ldo, resid, tcs, s, x16(W)));
     else gemm_q6_ld(W, X, n, out, ldo, resid, s);
     nl++;
   };
@@ -1014,10 +1038,10 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
       if (tc) {
         CK(tc_group(pgroups, n, n, tcs, s));
         CK(tc_split_grouped(ph, DIM, N_USED, n, tcs, s));
-        CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, n, pgate, tcs, s));
-        CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, n, pup, tcs, s));
+        CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, n, pgate, tcs, s, x16(L.gate_x)));
+        CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, n, pup, tcs, s, x16(L.up_x)));
         CK(tc_split_grouped(pgate, EXPERT_FF, 1, n, tcs, s, pup));  // SwiGLU fused into the operand split
-        CK(tc_gemm_q6_grouped(L.down_x, DIM, n, pdown, tcs, s));
+        CK(tc_gemm_q6_grouped(L.down_x, DIM, n, pdown, tcs, s, x16(L.down_x)));
         nl += 2;  // group layout, first split (the fused split stands in for SwiGLU)
       } else {
         gemm_q6_grouped(L.gate_x, EXPERT_FF, ph, N_USED, pgroups, n, n, pgate, s);
@@ -1110,10 +1134,10 @@ void EngineImpl::ep_moe(const LayerW& L, const float* rows, int n, float* xres) 
     expert_groups(ep_sel4, nf, pgroups, cap, s);
     CK(tc_group(pgroups, cap, nf, tcs, s));
     CK(tc_split_grouped(ep_recv, DIM, 1, nf, tcs, s));
-    CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, nf, pgate, tcs, s));
-    CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, nf, pup, tcs, s));
+    CK(tc_gemm_q6_grouped(L.gate_x, EXPERT_FF, nf, pgate, tcs, s, x16(L.gate_x)));
+    CK(tc_gemm_q6_grouped(L.up_x, EXPERT_FF, nf, pup, tcs, s, x16(L.up_x)));
     CK(tc_split_grouped(pgate, EXPERT_FF, 1, nf, tcs, s, pup));  // SwiGLU fused into the operand split
-    CK(tc_gemm_q6_grouped(L.down_x, DIM, nf, pdown, tcs, s));
+    CK(tc_gemm_q6_grouped(L.down_x, DIM, nf, pdown, tcs, s, x16(L.down_x)));
     ctr.expert_grouped_launches += 3;
   }
   // down rows back to the ranks that sent the slots, in the order they came
@@ -1275,7 +1299,7 @@ void EngineImpl::batch_prefill_many(const uint32_t* sess, const uint32_t* ids, c
                        cudaMemcpyDeviceToDevice, s));
   if (use_tc && count >= tc_min) {
     CK(tc_split_norm(ph, out_norm, eps, count, pa, tcs, s));
-    CK(tc_gemm_q6(embd, count, B.logits, (int)hp.vocab, false, tcs, s));
+    CK(tc_gemm_q6(embd, count, B.logits, (int)hp.vocab, false, tcs, s, x16(embd)));
   } else {
     rmsnorm_n(ph, out_norm, eps, count, pa, s);
     gemm_q6_ld(embd, pa, count, B.logits, (int)hp.vocab, false, s);
@@ -1328,7 +1352,7 @@ void EngineImpl::run_batch_decode(uint32_t count, const uint32_t* tokens, const 
   // final norm + tied lm_head for every token, then the row argmax
   if (use_tc && n >= tc_min) {
     CK(tc_split_norm(px, out_norm, eps, n, ph, tcs, s));
-    CK(tc_gemm_q6(embd, n, B.logits, (int)hp.vocab, false, tcs, s));
+    CK(tc_gemm_q6(embd, n, B.logits, (int)hp.vocab, false, tcs, s, x16(embd)));
   } else {
     rmsnorm_n(px, out_norm, eps, n, ph, s);
     gemm_q6_ld(embd, ph, n, B.logits, (int)hp.vocab, false, s);
@@ -1517,6 +1541,7 @@ lfm_status lfm_engine_create(const char* gguf_path, int device, lfm_engine** out
   if (const char* v = getenv("LFM_MVT")) I.use_mvt = std::string(v) != "0";
   if (const char* v = getenv("LFM_STEP")) I.use_step = std::string(v) != "0";
   if (const char* v = getenv("LFM_PREFILL")) I.use_tc = std::string(v) != "fp32";
+  if (const char* v = getenv("LFM_PREFILL_X16")) I.use_x16 = std::string(v) != "0";
   if (const char* v = getenv("LFM_TC_MIN_TOKENS")) I.tc_min = std::max(1, atoi(v));
   if (!I.use_step) I.step_reason = "persistent step disabled (LFM_STEP=0)";
   if (cudaStreamCreateWithFlags(&I.stream, cudaStreamNonBlocking) != cudaSuccess ||

@@ -307,6 +307,7 @@ struct TcQ6Params {
   const int* tiles;    // grouped: [0] = count, then (expert, first row) pairs
   const int* slots;    // grouped: operand row -> output slot (-1: padding)
   int grouped;
+  int tiles_y;         // dense: token tiles (the expanded-weight kernel's tile space)
   int ksplit;          // dense, one token tile: super-blocks split over blockIdx.z
   float* part;         // ... partial sums [ksplit][ntok][W.rows], reduced by k_tc_reduce
   unsigned* err;
@@ -618,6 +619,282 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(QTMEM_COLS));
+  }
+}
+
+// ======================================================================
+// Q6_K prompt GEMM over load-time expanded weights (the default when the
+// engine holds them): the A operand is the same fp16 integers sc*(q-32) that
+// k_tc_q6's workers make on chip, written once at load time into an fp16
+// matrix [rows][K] (q6_expand_f16), so the tile's A chunks arrive by TMA like
+// its activation chunks and no warp dequantises. Same MMAs, same
+// per-super-block TMEM accumulators, same fold y += d * (hi + lo) and the same
+// stores, so the results are bit-identical to k_tc_q6's.
+//   warp 0        TMA: lane 0 the activation chunks (as k_tc_q6), lane 1 the
+//                 A chunks (64-wide K x 128 rows, 128-byte swizzle)
+//   warp 1        TMEM allocation and the MMA issue (as k_tc_q6)
+//   warps 2-9     fold each super-block's accumulator as soon as it is complete,
+//                 then store
+__host__ __device__ constexpr int x_astages(int tt) { return tt >= 128 ? 4 : (tt >= 64 ? 4 : (tt >= 32 ? 4 : 3)); }
+__host__ __device__ constexpr int x_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 6)); }
+__host__ __device__ constexpr int x_off_b(int tt) { return x_astages(tt) * QA_BYTES; }
+__host__ __device__ constexpr int x_smem(int tt) { return x_off_b(tt) + x_bstages(tt) * 2 * tt * 128 + 1024; }
+static_assert(x_smem(128) <= 232448 - 2048 && x_smem(64) <= 232448 - 2048 && x_smem(32) <= 232448 - 2048 &&
+                  x_smem(16) <= 110 * 1024,
+              "expanded-weight GEMM shared memory");
+
+template <int TT>
+__global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
+    k_tc_q6x(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
+  constexpr int QB_BYTES = 2 * TT * 128;
+  constexpr uint32_t QTMEM_COLS = q_tmem_cols(TT);
+  constexpr uint32_t IDESC_Q = idesc_f16(128, 2 * TT, false);
+  constexpr int TH = TT / 2;  // tokens of one worker thread
+  constexpr int ASTAGES = x_astages(TT), BSTAGES = x_bstages(TT);
+  constexpr int NACC = q_nacc(TT);
+  constexpr int OFF_B = x_off_b(TT);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ uint64_t bfull[BSTAGES], bempty[BSTAGES], afull[ASTAGES], aempty[ASTAGES], acc_full[NACC],
+      acc_empty[NACC], mma_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ float s_inv[TT];
+  __shared__ int s_slot[TT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.W.nb;
+  // Persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ... of the
+  // (weight tile, token tile, K split) space, weight tiles fastest. Every ring
+  // and accumulator counter runs on across its tiles, so the next tile's
+  // loads and first MMAs proceed while the workers fold and store this one.
+  const int tiles_x = p.out_rows / 128;
+  const int tiles_y = p.grouped ? p.tiles[0] : p.tiles_y;
+  const int ntile = tiles_x * tiles_y * p.ksplit;
+  auto tile_of = [&](int t, int& o0, int& brow0, int& wrow0, int& kb0, int& nbl, int& z) {
+    const int x = t % tiles_x, r = t / tiles_x, y = r % tiles_y;
+    z = r / tiles_y;
+    o0 = x * 128;
+    if (p.grouped) {
+      wrow0 = p.tiles[1 + 2 * y] * p.out_rows;
+      brow0 = p.tiles[2 + 2 * y];
+    } else {
+      wrow0 = 0;
+      brow0 = y * TT;
+    }
+    kb0 = (int)((long long)z * nb / p.ksplit);
+    nbl = (int)((long long)(z + 1) * nb / p.ksplit) - kb0;
+  };
+  if ((int)blockIdx.x >= ntile) return;  // whole CTA leaves before any barrier or TMEM use
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BSTAGES; s++) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < ASTAGES; s++) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int r = 0; r < NACC; r++) {
+      mbar_init(&acc_full[r], 1);
+      mbar_init(&acc_empty[r], 8);
+    }
+    mbar_init(&mma_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&tmem_base, QTMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 || lane == 1) {
+      // lane 0: activation chunks (hi and lo rows); lane 1: A chunks
+      const bool act = lane == 0;
+      const int NS = act ? BSTAGES : ASTAGES;
+      uint64_t* full = act ? bfull : afull;
+      uint64_t* empty = act ? bempty : aempty;
+      int j = 0;  // chunks issued (all tiles)
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntile && ok; t += gridDim.x) {
+        int o0, brow0, wrow0, kb0, nbl, z;
+        tile_of(t, o0, brow0, wrow0, kb0, nbl, z);
+        for (int c = 0; c < 4 * nbl; c++, j++) {
+          const int s = j % NS, round = j / NS;
+          if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1, p.err))) break;
+          const int kx = 64 * (4 * kb0 + c);
+          if (act) {
+            uint8_t* bs = smem + OFF_B + s * QB_BYTES;
+            mbar_expect_tx(&full[s], QB_BYTES);
+            tma_load_2d(bs, &mapX, kx, brow0, &full[s]);
+            tma_load_2d(bs + QB_BYTES / 2, &mapX, kx, p.rpad + brow0, &full[s]);
+          } else {
+            mbar_expect_tx(&full[s], QA_BYTES);
+            tma_load_2d(smem + s * QA_BYTES, &mapA, kx, wrow0 + o0, &full[s]);
+          }
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      for (int k = j > NS ? j - NS : 0; k < j; k++) mbar_wait(&full[k % NS], (k / NS) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // -------------------------------------------------------------- MMA
+      bool ok = true;
+      int sb = 0, sa = 0, bg = 0;  // bg: super-blocks issued (all tiles)
+      uint32_t pb = 0, pa = 0;
+      const uint64_t dA0 = smem_desc_sw128(smem_u32(smem)), dB0 = smem_desc_sw128(smem_u32(smem + OFF_B));
+      for (int t = blockIdx.x; t < ntile && ok; t += gridDim.x) {
+        int o0, brow0, wrow0, kb0, nbl, z;
+        tile_of(t, o0, brow0, wrow0, kb0, nbl, z);
+        for (int b = 0; b < nbl && ok; b++, bg++) {
+          const int a = bg % NACC;
+          if (bg >= NACC && !(ok = mbar_wait(&acc_empty[a], ((bg / NACC) - 1) & 1, p.err))) break;
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(a * 2 * TT);
+          for (int c = 0; c < 4 && ok; c++) {
+            ok = mbar_wait(&bfull[sb], pb, p.err) && mbar_wait(&afull[sa], pa, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t da = dA0 + (uint64_t)((sa * QA_BYTES) >> 4), db = dB0 + (uint64_t)((sb * QB_BYTES) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) mma_f16(d, da + 2 * kk, db + 2 * kk, IDESC_Q, (c | kk) ? 1u : 0u);
+            mma_commit(&bempty[sb]);
+            mma_commit(&aempty[sa]);
+            if (++sb == BSTAGES) sb = 0, pb ^= 1u;
+            if (++sa == ASTAGES) sa = 0, pa ^= 1u;
+          }
+          mma_commit(&acc_full[a]);
+        }
+      }
+      mma_commit(&mma_done);
+      mbar_wait(&mma_done, 0, nullptr);
+    }
+  } else {
+    // --------------------------------------------------------------- workers
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(TH * g);
+    const int wt = threadIdx.x - 64;  // 0..255
+    bool ok = true;
+    int bg = 0;  // super-blocks folded (all tiles)
+    // Every worker warp walks every tile, also after a wait gave up, so that
+    // all of them meet the same named barriers.
+    for (int t = blockIdx.x; t < ntile; t += gridDim.x) {
+      int o0, brow0, wrow0, kb0, nbl, zk;  // zk: this tile's K split
+      tile_of(t, o0, brow0, wrow0, kb0, nbl, zk);
+      const size_t wrow = (size_t)wrow0 + o0 + row;
+      // the tile's row scales and slots (the previous tile's stores are done:
+      // every worker has passed this barrier after them)
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (wt < TT) {
+        s_inv[wt] = __ldg(p.inv + brow0 + wt);
+        s_slot[wt] = p.grouped ? __ldg(p.slots + brow0 + wt) : -1;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      float y[TH];
+#pragma unroll
+      for (int jj = 0; jj < TH; jj++) y[jj] = 0.f;
+      float dnext = __half2float(p.W.d[wrow * nb + kb0]);
+      for (int b = 0; b < nbl && ok; b++, bg++) {
+        // y += d_b * (hi + lo) for super-block b's accumulator, as soon as it is complete
+        const float d = dnext;
+        if (b + 1 < nbl) dnext = __half2float(p.W.d[wrow * nb + kb0 + b + 1]);
+        const int a = bg % NACC;
+        ok = mbar_wait(&acc_full[a], (bg / NACC) & 1, p.err);
+        tc_fence_after();
+        const uint32_t base = lane_base + (uint32_t)(a * 2 * TT);
+        if constexpr (TH >= 16) {
+#pragma unroll
+          for (int h = 0; h < TH / 16; h++) {
+            uint32_t hi[16], lo[16];
+            tmem_ld16_nowait(base + 16 * h, hi);
+            tmem_ld16_nowait(base + TT + 16 * h, lo);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++)
+              y[16 * h + jj] = fmaf(d, __uint_as_float(hi[jj]) + __uint_as_float(lo[jj]), y[16 * h + jj]);
+          }
+        } else {
+          uint32_t hi[8], lo[8];
+          tmem_ld8_nowait(base, hi);
+          tmem_ld8_nowait(base + TT, lo);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++) y[jj] = fmaf(d, __uint_as_float(hi[jj]) + __uint_as_float(lo[jj]), y[jj]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);
+      }
+      if (!ok) continue;
+      const int o = o0 + row;
+      const int bq = brow0 + TH * g;
+      constexpr int JC = TH < 16 ? TH : 16;
+#pragma unroll
+      for (int j0 = 0; j0 < TH; j0 += JC) {
+        float v[JC];
+#pragma unroll
+        for (int jj = 0; jj < JC; jj++) v[jj] = __fmul_rn(y[j0 + jj], s_inv[TH * g + j0 + jj]);
+        if (p.grouped) {
+#pragma unroll
+          for (int jj = 0; jj < JC; jj++) {
+            const int slot = s_slot[TH * g + j0 + jj];
+            if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v[jj];
+          }
+        } else if (p.part) {
+#pragma unroll
+          for (int jj = 0; jj < JC; jj++)
+            if (bq + j0 + jj < p.ntok) p.part[((size_t)zk * p.ntok + bq + j0 + jj) * p.W.rows + o] = v[jj];
+        } else if (p.resid) {
+          float old[JC];
+#pragma unroll
+          for (int jj = 0; jj < JC; jj++)
+            old[jj] = bq + j0 + jj < p.ntok ? p.out[(size_t)(bq + j0 + jj) * p.ldo + o] : 0.f;
+#pragma unroll
+          for (int jj = 0; jj < JC; jj++)
+            if (bq + j0 + jj < p.ntok) p.out[(size_t)(bq + j0 + jj) * p.ldo + o] = __fadd_rn(old[jj], v[jj]);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < JC; jj++)
+            if (bq + j0 + jj < p.ntok) p.out[(size_t)(bq + j0 + jj) * p.ldo + o] = v[jj];
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(QTMEM_COLS));
+  }
+}
+
+// Load-time expansion of a Q6_K matrix into the fp16 A operand of k_tc_q6x:
+// out[row][k] = fp16(sc * (q - 32)), rounded to nearest even like k_tc_q6's
+// on-chip __hmul2 (exact whenever |sc * (q - 32)| <= 2048 or even). One thread
+// per 64-weight unit.
+__global__ void k_q6_expand_f16(Q6Mat W, __half* out) {
+  const int U = 4 * W.nb;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)W.rows * U) return;
+  const size_t row = i / U;
+  const int u = (int)(i % U);
+  const uint4* qp = W.q + row * 3 * U + u;
+  const uint4 A = qp[0], B = qp[U], Q = qp[2 * U];
+  const uint32_t scw = W.sc[row * U + u];
+  const uint32_t a[4] = {A.x, A.y, A.z, A.w}, b[4] = {B.x, B.y, B.z, B.w}, q[4] = {Q.x, Q.y, Q.z, Q.w};
+  __half* dst = out + row * (size_t)(W.nb * QK) + q6_unit_base(u);
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    uint32_t w[4];
+    q6_words(a[t], b[t], q[t], w[0], w[1], w[2], w[3]);
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      const float sc = sc_val(scw, m);
+#pragma unroll
+      for (int j = 0; j < 4; j++) dst[32 * m + 4 * t + j] = __float2half_rn(sc * q6_val(w[m], j));
+    }
   }
 }
 
@@ -936,8 +1213,42 @@ cudaError_t launch_q6_tt(const CUtensorMap& mq, const CUtensorMap& ms, const CUt
   return cudaGetLastError();
 }
 
+template <int TT>
+cudaError_t launch_q6x_tt(const CUtensorMap& ma, const CUtensorMap& mx, dim3 grid, const TcQ6Params& p,
+                          cudaStream_t s) {
+  static unsigned long long done = 0;
+  static std::mutex mu;
+  once_per_device(done, mu,
+                  [] { cudaFuncSetAttribute(k_tc_q6x<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, x_smem(TT)); });
+  k_tc_q6x<TT><<<grid, QTHREADS, x_smem(TT), s>>>(ma, mx, p);
+  return cudaGetLastError();
+}
+
+// the expanded-weight kernel when x16 (the load-time fp16 A operand of W) is given
 cudaError_t launch_q6(const Q6Mat& W, int rpad, int tt, int ntiles_y, const TcQ6Params& p, const TcScratch& sc,
-                      cudaStream_t s) {
+                      cudaStream_t s, const __half* x16 = nullptr) {
+  if (x16) {
+    CUtensorMap ma, mx;
+    cudaError_t e = tc_map_f16(&ma, x16, W.rows, W.nb * QK, 128);
+    if (e != cudaSuccess) return e;
+    e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, tt);
+    if (e != cudaSuccess) return e;
+    // persistent: at most one wave of CTAs walks every tile
+    TcQ6Params q = p;
+    q.tiles_y = ntiles_y;
+    const long long ntile = (long long)(p.out_rows / 128) * ntiles_y * p.ksplit;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const dim3 grid((unsigned)std::min<long long>(ntile, (long long)sms * q_ctas_per_sm(tt)));
+    switch (tt) {
+      case 16: return launch_q6x_tt<16>(ma, mx, grid, q, s);
+      case 32: return launch_q6x_tt<32>(ma, mx, grid, q, s);
+      case 64: return launch_q6x_tt<64>(ma, mx, grid, q, s);
+      case 128: return launch_q6x_tt<128>(ma, mx, grid, q, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   CUtensorMap mq, ms, mx;
   cudaError_t e = map_raw(&mq, &ms, W);
   if (e != cudaSuccess) return e;
@@ -975,8 +1286,15 @@ cudaError_t tc_split_norm(const float* X, const float* w, float eps, int n, floa
   return cudaGetLastError();
 }
 
+cudaError_t q6_expand_f16(const Q6Mat& W, __half* out, cudaStream_t s) {
+  const size_t units = (size_t)W.rows * 4 * W.nb;
+  if (!out || units == 0) return cudaErrorInvalidValue;
+  k_q6_expand_f16<<<(unsigned)((units + 255) / 256), 256, 0, s>>>(W, out);
+  return cudaGetLastError();
+}
+
 cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
-                       cudaStream_t s) {
+                       cudaStream_t s, const __half* x16) {
   const int rpad = dense_rpad(n);
   if (n <= 0 || !fits(sc, rpad, W.nb * QK) || !tc_q6_supported(W, W.rows)) return cudaErrorInvalidValue;
   TcQ6Params p = {};
@@ -1000,14 +1318,14 @@ cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, c
     if (ks > 1) {
       p.ksplit = ks;
       p.part = sc.part;
-      cudaError_t e = launch_q6(W, rpad, tt, 1, p, sc, s);
+      cudaError_t e = launch_q6(W, rpad, tt, 1, p, sc, s, x16);
       if (e != cudaSuccess) return e;
       const size_t cnt = (size_t)n * W.rows;
       k_tc_reduce<<<(unsigned)((cnt + 255) / 256), 256, 0, s>>>(sc.part, ks, n, W.rows, out, ldo, resid ? 1 : 0);
       return cudaGetLastError();
     }
   }
-  return launch_q6(W, rpad, tt, rpad / tt, p, sc, s);
+  return launch_q6(W, rpad, tt, rpad / tt, p, sc, s, x16);
 }
 
 cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cudaStream_t s) {
@@ -1029,7 +1347,7 @@ cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcSc
 }
 
 cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, const TcScratch& sc,
-                               cudaStream_t s) {
+                               cudaStream_t s, const __half* x16) {
   const int rpad = grouped_rpad(n);
   if (n <= 0 || !fits(sc, rpad, W.nb * QK) || !tc_q6_supported(W, out_rows) || W.rows / out_rows > N_EXPERT)
     return cudaErrorInvalidValue;
@@ -1045,7 +1363,7 @@ cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, 
   p.grouped = 1;
   p.err = sc.err;
   p.ksplit = 1;
-  return launch_q6(W, rpad, grouped_tt(n), tc_max_tiles(n), p, sc, s);
+  return launch_q6(W, rpad, grouped_tt(n), tc_max_tiles(n), p, sc, s, x16);
 }
 
 int tc_max_tiles(int n) {

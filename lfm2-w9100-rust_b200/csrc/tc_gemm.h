@@ -63,8 +63,13 @@ cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc,
 // fused with the split of the normalised rows into the operand.
 cudaError_t tc_split_norm(const float* X, const float* w, float eps, int n, float* normed, const TcScratch& sc,
                           cudaStream_t s);
+// x16 (optional): W expanded at load time into its fp16 A operand
+// (q6_expand_f16); the GEMM then loads A by TMA instead of dequantising on chip.
 cudaError_t tc_gemm_q6(const Q6Mat& W, int n, float* out, int ldo, bool resid, const TcScratch& sc,
-                       cudaStream_t s);
+                       cudaStream_t s, const __half* x16 = nullptr);
+// The fp16 A operand of W's prompt GEMMs: out[row][k] = fp16(sc * (q - 32))
+// ([W.rows][W.nb * 256], 2 bytes per weight).
+cudaError_t q6_expand_f16(const Q6Mat& W, __half* out, cudaStream_t s);
 
 // Routed experts: tc_group lays out the expert lists (groups[e * (cap + 1)] =
 // count, then selection slots t * 4 + rank), tc_split_grouped fills operand
@@ -74,6 +79,6 @@ cudaError_t tc_group(const int* groups, int cap, int n, const TcScratch& sc, cud
 cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcScratch& sc, cudaStream_t s,
                              const float* up = nullptr);
 cudaError_t tc_gemm_q6_grouped(const Q6Mat& W, int out_rows, int n, float* out, const TcScratch& sc,
-                               cudaStream_t s);
+                               cudaStream_t s, const __half* x16 = nullptr);
 
 }  // namespace lfm

@@ -43,3 +43,32 @@ def test_prefill_logits_vs_oracle(engine, synth_model, oracle_mod, n):
     top = np.sort(ref)[-2:]
     if top[1] - top[0] > 2 * err:
         assert int(np.argmax(got)) == int(np.argmax(ref))
+
+
+def test_expanded_weights_bit_identical(engine, synth_model):
+    """The prompt GEMMs over load-time expanded fp16 weights (the default)
+    compute exactly what the on-chip dequantising GEMMs compute
+    (LFM_PREFILL_X16=0): same A operand values, MMAs and fold."""
+    import os
+
+    import lfm2_b200
+    old = os.environ.get("LFM_PREFILL_X16")
+    os.environ["LFM_PREFILL_X16"] = "0"
+    try:
+        plain = lfm2_b200.GpuEngine(synth_model, 0)
+    finally:
+        if old is None:
+            del os.environ["LFM_PREFILL_X16"]
+        else:
+            os.environ["LFM_PREFILL_X16"] = old
+    try:
+        for n in (2, 17, 200, 1000):
+            p = np.random.default_rng(2000 + n).integers(0, 128000, n).astype(np.uint32)
+            outs = []
+            for e in (engine, plain):
+                e.set_ctx(1024 + 16)
+                e.reset_session()
+                outs.append(e.forward(p, 0))
+            assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32)), n
+    finally:
+        plain.close()
