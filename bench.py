@@ -269,6 +269,71 @@ def microbench(device: int) -> list:
     return out
 
 
+def prompt_gemm_bench(device: int, n: int, reps: int = 5) -> list:
+    """The prompt path's Q6_K GEMMs for an n-token prefill through the
+    kernel-level C ABI, with the weight operand expanded to fp16 ahead of time
+    (what the engine does at load): activation split + tensor-core GEMM per
+    call, CUDA events on the launching stream. Routed rows send each token to
+    4 of 32 experts (seeded, uniform); their FLOPs count the 4 n routed rows.
+    Random Q6_K bytes with plausible super-block scales; the expert matrices'
+    fp16 operands (235 MB) are larger than L2, the dense ones are not."""
+    import ctypes
+
+    import torch
+
+    import lfm2_b200
+    lib = lfm2_b200.lib()
+    torch.cuda.set_device(device)
+    s = torch.cuda.current_stream()
+    st = ctypes.c_void_p(s.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    peak = measured_peaks()["bf16_tflops"]
+    rng = np.random.default_rng(n)
+    # routed down first: `ncu -k regex:k_tc_q6x -c 1` on this mode captures it
+    shapes = [("routed down 1792->2048, grouped", 1792, 2048, 1), ("routed gate 2048->1792, grouped", 2048, 1792, 4),
+              ("conv in_proj 2048->6144", 2048, 6144, 0), ("attn/conv out 2048->2048", 2048, 2048, 0),
+              ("dense gate 2048->7168", 2048, 7168, 0), ("dense down 7168->2048", 7168, 2048, 0)]
+    out = []
+    for name, ind, outd, x_div in shapes:
+        mrows = outd * 32 if x_div else outd
+        nbytes = lib.lfm_q6k_device_bytes(ind, mrows)
+        g = torch.Generator(device="cuda").manual_seed(2)
+        w = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda", generator=g)
+        w.view(-1)[-(nbytes // 105):].bitwise_and_(0x3B)  # plausible fp16 d values
+        w16 = torch.empty((mrows, ind), dtype=torch.float16, device="cuda")
+        lfm2_b200.ops_check(lib.lfm_q6k_expand_f16(P(w), ind, mrows, P(w16), st), "expand_f16")
+        if x_div:
+            ids = torch.from_numpy(np.stack([rng.permutation(32)[:4] for _ in range(n)]).astype(np.int32)).cuda()
+            x = torch.randn((n if x_div == 4 else 4 * n) * ind, device="cuda")
+            y = torch.empty(4 * n * outd, device="cuda")
+
+            def call():
+                return lib.lfm_q6k_prompt_grouped_x16(P(w), P(w16), ind, outd, 32, P(ids), P(x), x_div, n, P(y), st)
+            flop = 2.0 * 4 * n * ind * outd
+        else:
+            x = torch.randn(n * ind, device="cuda")
+            y = torch.empty(n * outd, device="cuda")
+
+            def call():
+                return lib.lfm_q6k_prompt_gemm_x16(P(w), P(w16), ind, outd, P(x), n, P(y), st)
+            flop = 2.0 * n * ind * outd
+        lfm2_b200.ops_check(call(), name)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            lfm2_b200.ops_check(call(), name)
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / reps
+        tf = flop / us / 1e6
+        out.append({"shape": name, "tokens": n, "us_per_call": round(us, 1), "tflops": round(tf, 1),
+                    "frac_of_bf16_peak": round(tf / peak, 4)})
+        del w, w16
+        torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline(path: str, steps: int, warmup: int, threads: int | None = None, one_core_steps: int = 3) -> dict:
     """The oracle on the host cores: 512-token prefill (untimed setup), `warmup`
     untimed and `steps` timed greedy decode steps at 512+ context on `threads`
@@ -603,6 +668,8 @@ def main():
     ap.add_argument("--sessions-only", action="store_true", help="only config 4 on this GPU (profiling entry point)")
     ap.add_argument("--prefill-only", type=int, default=0, metavar="N",
                     help="only one warm-up and one timed N-token prefill (profiling entry point)")
+    ap.add_argument("--prompt-gemm", type=int, default=0, metavar="N",
+                    help="only the prompt GEMMs of an N-token prefill through the C ABI (profiling entry point)")
     ap.add_argument("--step-trace", type=int, default=0, metavar="N",
                     help="only the decode step's stage timeline after an N-token prompt (profiling entry point)")
     args = ap.parse_args()
@@ -615,6 +682,10 @@ def main():
     if args.prefill_only:
         if rank == 0:
             print(json.dumps(prefill_only(local, args.prefill_only)), flush=True)
+        return
+    if args.prompt_gemm:
+        if rank == 0:
+            print(json.dumps({"prompt_gemm": prompt_gemm_bench(local, args.prompt_gemm)}), flush=True)
         return
     if args.step_trace:
         if rank == 0:
@@ -730,9 +801,10 @@ def main():
     ep = None
     if ws > 1 and not args.no_ep:
         ep = ep_compare(eng, pg, ws, rank)
-    micro = None
+    micro = pgemm = None
     if rank == 0 and not args.no_micro:
         micro = microbench(local)
+        pgemm = prompt_gemm_bench(local, PREFILL_LEN)
     cpu = None
     eng.close()  # release the device before the CPU leg and before interpreter teardown
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -745,7 +817,7 @@ def main():
                 "config": workload_config(ws), "decode_path": path_name,
                 "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "prefill": prefill, "multi_session": multi, "expert_parallel_prefill": ep,
-                "microbench": micro, "cpu_baseline": cpu,
+                "microbench": micro, "prompt_gemm_microbench": pgemm, "cpu_baseline": cpu,
                 "tokens_head": toks[:8]}
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -361,6 +361,25 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
                                   const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_div,
                                   uint32_t n, float* y_dev, void* stream);
 
+/* The prompt GEMMs' weight operand expanded ahead of time: out_dev (fp16,
+ * [rows][in_dim], 2 bytes per weight, 16-byte aligned) receives the exact
+ * integers sc*(q-32) of every weight (q6k.rs:74-146 without the super-block
+ * scale d, which the GEMM applies per super-block). The engine builds this
+ * operand for every Q6_K matrix when it loads a model (unless
+ * LFM_PREFILL_X16=0 or the device lacks the room). No counterpart in the
+ * reference, whose prompt kernels dequantise on the fly. Asynchronous on
+ * `stream`. */
+lfm_status lfm_q6k_expand_f16(const void* w_dev, uint32_t in_dim, uint32_t rows, void* out_dev, void* stream);
+
+/* lfm_q6k_prompt_gemm and lfm_q6k_prompt_grouped reading their weight
+ * operand from w16_dev (lfm_q6k_expand_f16 of w_dev; w_dev still supplies the
+ * super-block scales d). Same contracts and results, bit for bit. */
+lfm_status lfm_q6k_prompt_gemm_x16(const void* w_dev, const void* w16_dev, uint32_t in_dim, uint32_t rows,
+                                   const float* x_dev, uint32_t n, float* y_dev, void* stream);
+lfm_status lfm_q6k_prompt_grouped_x16(const void* w_dev, const void* w16_dev, uint32_t in_dim, uint32_t rows,
+                                      uint32_t n_expert, const int32_t* expert_ids_dev, const float* x_dev,
+                                      uint32_t x_div, uint32_t n, float* y_dev, void* stream);
+
 /* Failure-detection self-test (no counterpart in the reference, whose
  * watchdog handling is vulkan/fence_stop.rs): one thread waits on an
  * mbarrier that nothing completes, through the library's bounded wait (about

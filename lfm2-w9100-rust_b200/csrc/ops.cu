@@ -249,6 +249,60 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
   return cs.finish(e, "lfm_q6k_prompt_grouped");
 }
 
+lfm_status lfm_q6k_expand_f16(const void* w_dev, uint32_t in_dim, uint32_t rows, void* out_dev, void* stream) {
+  if (!w_dev || !out_dev || !shape_ok(in_dim, rows) || (uintptr_t)out_dev % 16) {
+    t_err = "lfm_q6k_expand_f16: bad argument (out_dev 16-byte aligned)";
+    return LFM_ERR_ARG;
+  }
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
+  return cuda_status(lfm::q6_expand_f16(W, (__half*)out_dev, (cudaStream_t)stream));
+}
+
+lfm_status lfm_q6k_prompt_gemm_x16(const void* w_dev, const void* w16_dev, uint32_t in_dim, uint32_t rows,
+                                   const float* x_dev, uint32_t n, float* y_dev, void* stream) {
+  if (!w_dev || !w16_dev || !x_dev || !y_dev || !shape_ok(in_dim, rows) || rows % 128 || n == 0 ||
+      n > (1u << 20) || (uintptr_t)w16_dev % 16) {
+    t_err = "lfm_q6k_prompt_gemm_x16: bad argument (rows % 128 == 0, 1 <= n <= 2^20, w16_dev 16-byte aligned)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)rows, (int)(in_dim / 256));
+  CallScratch cs(s);
+  cudaError_t e = cs.alloc((n + 127) / 128 * 128, in_dim, 1);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) e = lfm::tc_split(x_dev, (int)in_dim, (int)in_dim, (int)n, cs.sc, s);
+  if (e == cudaSuccess) e = lfm::tc_gemm_q6(W, (int)n, y_dev, (int)rows, false, cs.sc, s, (const __half*)w16_dev);
+  return cs.finish(e, "lfm_q6k_prompt_gemm_x16");
+}
+
+lfm_status lfm_q6k_prompt_grouped_x16(const void* w_dev, const void* w16_dev, uint32_t in_dim, uint32_t rows,
+                                      uint32_t n_expert, const int32_t* expert_ids_dev, const float* x_dev,
+                                      uint32_t x_div, uint32_t n, float* y_dev, void* stream) {
+  if (!w_dev || !w16_dev || !x_dev || !y_dev || !expert_ids_dev || !shape_ok(in_dim, rows) || rows % 128 ||
+      n_expert != (uint32_t)lfm::N_EXPERT || (x_div != 1 && x_div != (uint32_t)lfm::N_USED) || n == 0 ||
+      n > (1u << 16) || (uintptr_t)w16_dev % 16) {
+    t_err = "lfm_q6k_prompt_grouped_x16: bad argument (rows % 128 == 0, n_expert == 32, x_div 1 or 4, "
+            "1 <= n <= 65536, w16_dev 16-byte aligned)";
+    return LFM_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  lfm::Q6Mat W = lfm::q6_view(w_dev, (int)(rows * n_expert), (int)(in_dim / 256));
+  CallScratch cs(s);
+  int* groups = nullptr;
+  cudaError_t e = cs.alloc(lfm::tc_scratch_rows((int)n), in_dim, (size_t)n * lfm::N_USED);
+  if (e == cudaSuccess) e = cudaMallocAsync(&groups, sizeof(int) * (size_t)lfm::N_EXPERT * (n + 1), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
+  if (e == cudaSuccess) {
+    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s);
+    e = lfm::tc_group(groups, (int)n, (int)n, cs.sc, s);
+  }
+  if (e == cudaSuccess) e = lfm::tc_split_grouped(x_dev, (int)in_dim, (int)x_div, (int)n, cs.sc, s);
+  if (e == cudaSuccess)
+    e = lfm::tc_gemm_q6_grouped(W, (int)rows, (int)n, y_dev, cs.sc, s, (const __half*)w16_dev);
+  if (groups) cudaFreeAsync(groups, s);
+  return cs.finish(e, "lfm_q6k_prompt_grouped_x16");
+}
+
 lfm_status lfm_attention_prefill(const float* q_dev, uint32_t q_stride, const void* k_cache, const void* v_cache,
                                  uint32_t ctx, uint32_t start, uint32_t n, float* out_dev, uint32_t out_stride,
                                  void* stream) {

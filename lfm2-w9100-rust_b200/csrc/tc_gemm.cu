@@ -25,7 +25,9 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "dev_common.cuh"
 #include "host_once.h"
@@ -635,8 +637,18 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
 //   warp 1        TMEM allocation and the MMA issue (as k_tc_q6)
 //   warps 2-9     fold each super-block's accumulator as soon as it is complete,
 //                 then store
-__host__ __device__ constexpr int x_astages(int tt) { return tt >= 128 ? 4 : (tt >= 64 ? 4 : (tt >= 32 ? 4 : 3)); }
-__host__ __device__ constexpr int x_bstages(int tt) { return tt >= 128 ? 5 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 6)); }
+#ifndef LFM_X_A128
+#define LFM_X_A128 4
+#endif
+#ifndef LFM_X_B128
+#define LFM_X_B128 5
+#endif
+__host__ __device__ constexpr int x_astages(int tt) {
+  return tt >= 128 ? LFM_X_A128 : (tt >= 64 ? 4 : (tt >= 32 ? 4 : 3));
+}
+__host__ __device__ constexpr int x_bstages(int tt) {
+  return tt >= 128 ? LFM_X_B128 : (tt >= 64 ? 8 : (tt >= 32 ? 12 : 6));
+}
 __host__ __device__ constexpr int x_off_b(int tt) { return x_astages(tt) * QA_BYTES; }
 __host__ __device__ constexpr int x_smem(int tt) { return x_off_b(tt) + x_bstages(tt) * 2 * tt * 128 + 1024; }
 static_assert(x_smem(128) <= 232448 - 2048 && x_smem(64) <= 232448 - 2048 && x_smem(32) <= 232448 - 2048 &&
@@ -867,6 +879,288 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(QTMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM form of k_tc_q6x for 128-token tiles: a cluster of two CTAs (one per SM)
+// computes 256 weight rows x 128 tokens with tcgen05.mma.cta_group::2 (M=256,
+// N=256). CTA r of the pair holds weight rows [128 r, 128 r + 128) of the tile
+// (A) and one half of the activation operand (B): CTA 0 the hi rows, CTA 1 the
+// lo rows; its TMEM receives its 128 rows x all 256 columns (hi then lo), so
+// each CTA's workers fold and store exactly as k_tc_q6x's do. Per 64-wide K
+// chunk each SM loads 32 KB (16 KB of A, 16 KB of B) instead of 48 KB, which
+// buys a deeper ring in the same shared memory.
+//   Barriers: the leader (rank 0) owns the operand-full barriers; both CTAs'
+//   TMA loads complete their bytes on the leader's barrier (the .cta_group::2
+//   load form with the leader's barrier mapped by mapa), the leader's producer
+//   arms it for both. The leader's warp 1 issues the MMAs; its commits arrive
+//   on both CTAs' slot-empty and accumulator-full barriers (multicast commit).
+//   Both CTAs' workers release an accumulator on the leader's barrier (16
+//   arrivals). Every wait is bounded; a cluster barrier before teardown keeps
+//   each CTA alive while its peer may still signal it.
+constexpr int X2_ASTAGES = 7, X2_BSTAGES = 6;
+constexpr int X2_STAGE = 128 * 128;  // 128 rows x 64 fp16, either operand
+constexpr int X2_OFF_B = X2_ASTAGES * X2_STAGE;
+constexpr int X2_SMEM = X2_OFF_B + X2_BSTAGES * X2_STAGE + 1024;
+static_assert(X2_SMEM <= 232448 - 2048, "2-SM expanded-weight GEMM shared memory");
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of this CTA's shared variable `p` in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// TMA load into this CTA's shared memory completing on an mbarrier that may be
+// the peer CTA's (shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+// arrive on `bar` (same offset) in both CTAs of the pair once this thread's MMAs completed
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __launch_bounds__(QTHREADS, 1)
+    k_tc_q6x2(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
+  constexpr int TT = 128, TH = TT / 2;
+  constexpr uint32_t IDESC2 = idesc_f16(256, 2 * TT, false);
+  constexpr int NACC = 2;  // two 256-column accumulators: all 512 TMEM columns
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ uint64_t bfull[X2_BSTAGES], bempty[X2_BSTAGES], afull[X2_ASTAGES], aempty[X2_ASTAGES], acc_full[NACC],
+      acc_empty[NACC], mma_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ float s_inv[TT];
+  __shared__ int s_slot[TT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank_in_cluster();
+  const bool leader = rank == 0;
+  const int nb = p.W.nb;
+  // pairs walk the (256-row weight tile, token tile, K split) space, weight tiles fastest
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_x = p.out_rows / 256;
+  const int tiles_y = p.grouped ? p.tiles[0] : p.tiles_y;
+  const int ntile = tiles_x * tiles_y * p.ksplit;
+  auto tile_of = [&](int t, int& o0, int& brow0, int& wrow0, int& kb0, int& nbl, int& z) {
+    const int x = t % tiles_x, r = t / tiles_x, y = r % tiles_y;
+    z = r / tiles_y;
+    o0 = x * 256 + 128 * (int)rank;  // this CTA's 128 rows
+    if (p.grouped) {
+      wrow0 = p.tiles[1 + 2 * y] * p.out_rows;
+      brow0 = p.tiles[2 + 2 * y];
+    } else {
+      wrow0 = 0;
+      brow0 = y * TT;
+    }
+    kb0 = (int)((long long)z * nb / p.ksplit);
+    nbl = (int)((long long)(z + 1) * nb / p.ksplit) - kb0;
+  };
+  // both CTAs of a pair see the same tile count, so a pair leaves together
+  if (pair >= ntile) return;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < X2_BSTAGES; s++) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < X2_ASTAGES; s++) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int r = 0; r < NACC; r++) {
+      mbar_init(&acc_full[r], 1);
+      mbar_init(&acc_empty[r], 16);  // 8 worker warps in each CTA
+    }
+    mbar_init(&mma_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before anything signals them
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 || lane == 1) {
+      // lane 0: this CTA's half of the activation chunk; lane 1: its A chunk
+      const bool act = lane == 0;
+      const int NS = act ? X2_BSTAGES : X2_ASTAGES;
+      uint64_t* full = act ? bfull : afull;
+      uint64_t* empty = act ? bempty : aempty;
+      uint8_t* ring = smem + (act ? X2_OFF_B : 0);
+      int j = 0;
+      bool ok = true;
+      for (int t = pair; t < ntile && ok; t += npairs) {
+        int o0, brow0, wrow0, kb0, nbl, z;
+        tile_of(t, o0, brow0, wrow0, kb0, nbl, z);
+        for (int c = 0; c < 4 * nbl; c++, j++) {
+          const int s = j % NS, round = j / NS;
+          if (round > 0 && !(ok = mbar_wait(&empty[s], (round - 1) & 1, p.err))) break;
+          const int kx = 64 * (4 * kb0 + c);
+          if (leader) mbar_expect_tx(&full[s], 2 * X2_STAGE);  // both CTAs' bytes
+          const uint32_t bar = cluster_addr(&full[s], 0);
+          if (act)
+            tma_load_2d_pair(ring + s * X2_STAGE, &mapX, kx, (rank ? p.rpad : 0) + brow0, bar);
+          else
+            tma_load_2d_pair(ring + s * X2_STAGE, &mapA, kx, wrow0 + o0, bar);
+        }
+      }
+      // the leader's copies (and the peer's, which complete on the same
+      // barriers) land before the CTA may exit
+      if (leader)
+        for (int k = j > NS ? j - NS : 0; k < j; k++) mbar_wait(&full[k % NS], (k / NS) & 1, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      if (leader) {
+        // ------------------------------------------------------------ MMA
+        bool ok = true;
+        int sb = 0, sa = 0, bg = 0;
+        uint32_t pb = 0, pa = 0;
+        const uint64_t dA0 = smem_desc_sw128(smem_u32(smem)), dB0 = smem_desc_sw128(smem_u32(smem + X2_OFF_B));
+        for (int t = pair; t < ntile && ok; t += npairs) {
+          int o0, brow0, wrow0, kb0, nbl, z;
+          tile_of(t, o0, brow0, wrow0, kb0, nbl, z);
+          for (int b = 0; b < nbl && ok; b++, bg++) {
+            const int a = bg % NACC;
+            if (bg >= NACC && !(ok = mbar_wait(&acc_empty[a], ((bg / NACC) - 1) & 1, p.err))) break;
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(a * 2 * TT);
+            for (int c = 0; c < 4 && ok; c++) {
+              ok = mbar_wait(&bfull[sb], pb, p.err) && mbar_wait(&afull[sa], pa, p.err);
+              if (!ok) break;
+              tc_fence_after();
+              const uint64_t da = dA0 + (uint64_t)((sa * X2_STAGE) >> 4), db = dB0 + (uint64_t)((sb * X2_STAGE) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; kk++) mma_f16_pair(d, da + 2 * kk, db + 2 * kk, IDESC2, (c | kk) ? 1u : 0u);
+              mma_commit_pair(&bempty[sb]);
+              mma_commit_pair(&aempty[sa]);
+              if (++sb == X2_BSTAGES) sb = 0, pb ^= 1u;
+              if (++sa == X2_ASTAGES) sa = 0, pa ^= 1u;
+            }
+            mma_commit_pair(&acc_full[a]);
+          }
+        }
+        mma_commit_pair(&mma_done);
+      }
+      // both CTAs: the leader's MMAs (which read this CTA's operands) are done
+      mbar_wait(&mma_done, 0, nullptr);
+    }
+  } else {
+    // --------------------------------------------------------------- workers
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(TH * g);
+    const int wt = threadIdx.x - 64;
+    bool ok = true;
+    int bg = 0;
+    for (int t = pair; t < ntile; t += npairs) {
+      int o0, brow0, wrow0, kb0, nbl, zk;
+      tile_of(t, o0, brow0, wrow0, kb0, nbl, zk);
+      const size_t wrow = (size_t)wrow0 + o0 + row;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (wt < TT) {
+        s_inv[wt] = __ldg(p.inv + brow0 + wt);
+        s_slot[wt] = p.grouped ? __ldg(p.slots + brow0 + wt) : -1;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      float y[TH];
+#pragma unroll
+      for (int jj = 0; jj < TH; jj++) y[jj] = 0.f;
+      float dnext = __half2float(p.W.d[wrow * nb + kb0]);
+      for (int b = 0; b < nbl && ok; b++, bg++) {
+        const float d = dnext;
+        if (b + 1 < nbl) dnext = __half2float(p.W.d[wrow * nb + kb0 + b + 1]);
+        const int a = bg % NACC;
+        ok = mbar_wait(&acc_full[a], (bg / NACC) & 1, p.err);
+        tc_fence_after();
+        const uint32_t base = lane_base + (uint32_t)(a * 2 * TT);
+#pragma unroll
+        for (int h = 0; h < TH / 16; h++) {
+          uint32_t hi[16], lo[16];
+          tmem_ld16_nowait(base + 16 * h, hi);
+          tmem_ld16_nowait(base + TT + 16 * h, lo);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++)
+            y[16 * h + jj] = fmaf(d, __uint_as_float(hi[jj]) + __uint_as_float(lo[jj]), y[16 * h + jj]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(cluster_addr(&acc_empty[a], 0));
+      }
+      if (!ok) continue;
+      const int o = o0 + row;
+      const int bq = brow0 + TH * g;
+#pragma unroll
+      for (int j0 = 0; j0 < TH; j0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) v[jj] = __fmul_rn(y[j0 + jj], s_inv[TH * g + j0 + jj]);
+        if (p.grouped) {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) {
+            const int slot = s_slot[TH * g + j0 + jj];
+            if (slot >= 0) p.out[(size_t)slot * p.ldo + o] = v[jj];
+          }
+        } else if (p.part) {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++)
+            if (bq + j0 + jj < p.ntok) p.part[((size_t)zk * p.ntok + bq + j0 + jj) * p.W.rows + o] = v[jj];
+        } else if (p.resid) {
+          float old[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++)
+            old[jj] = bq + j0 + jj < p.ntok ? p.out[(size_t)(bq + j0 + jj) * p.ldo + o] : 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++)
+            if (bq + j0 + jj < p.ntok) p.out[(size_t)(bq + j0 + jj) * p.ldo + o] = __fadd_rn(old[jj], v[jj]);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++)
+            if (bq + j0 + jj < p.ntok) p.out[(size_t)(bq + j0 + jj) * p.ldo + o] = v[jj];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
@@ -1224,9 +1518,78 @@ cudaError_t launch_q6x_tt(const CUtensorMap& ma, const CUtensorMap& mx, dim3 gri
   return cudaGetLastError();
 }
 
+// Pairs of the 2-SM kernel that fit on the device at once (per device, once).
+int x2_max_pairs() {
+  static int cached[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int n = 0;
+  if (cudaFuncSetAttribute(k_tc_q6x2, cudaFuncAttributeMaxDynamicSharedMemorySize, X2_SMEM) == cudaSuccess &&
+      cudaFuncSetAttribute(k_tc_q6x2, cudaFuncAttributeNonPortableClusterSizeAllowed, 0) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(QTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = X2_SMEM;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, k_tc_q6x2, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  n = n > 0 ? n : -1;  // -1: the 2-SM kernel cannot run here
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+// LFM_PREFILL_2SM=1 moves 128-token tiles to the 2-SM kernel. Off by default:
+// measured on the prompt path it is bit-identical and no faster (3840 tokens
+// 32.5 vs 32.0 ms, 1024 tokens 12.1 vs 11.5 ms).
+bool x2_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LFM_PREFILL_2SM");
+    return v && std::string(v) == "1";
+  }();
+  return on;
+}
+
+cudaError_t launch_q6x2(const CUtensorMap& ma, const CUtensorMap& mx, int pairs, const TcQ6Params& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(QTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = X2_SMEM;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_tc_q6x2, ma, mx, p);
+}
+
 // the expanded-weight kernel when x16 (the load-time fp16 A operand of W) is given
 cudaError_t launch_q6(const Q6Mat& W, int rpad, int tt, int ntiles_y, const TcQ6Params& p, const TcScratch& sc,
                       cudaStream_t s, const __half* x16 = nullptr) {
+  if (x16 && tt == 128 && p.out_rows % 256 == 0 && x2_enabled() && x2_max_pairs() > 0) {
+    CUtensorMap ma, mx;
+    cudaError_t e = tc_map_f16(&ma, x16, W.rows, W.nb * QK, 128);
+    if (e != cudaSuccess) return e;
+    e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, 128);
+    if (e != cudaSuccess) return e;
+    TcQ6Params q = p;
+    q.tiles_y = ntiles_y;
+    const long long ntile = (long long)(p.out_rows / 256) * ntiles_y * p.ksplit;
+    const int pairs = (int)std::min<long long>(ntile, x2_max_pairs());
+    return launch_q6x2(ma, mx, pairs, q, s);
+  }
   if (x16) {
     CUtensorMap ma, mx;
     cudaError_t e = tc_map_f16(&ma, x16, W.rows, W.nb * QK, 128);

@@ -53,6 +53,7 @@ EXPORTS = [
     "lfm_device_name", "lfm_last_error", "lfm_global_error", "lfm_q6k_device_bytes",
     "lfm_q6k_upload", "lfm_q6k_dequant", "lfm_q6k_matmul", "lfm_q6k_routed", "lfm_route",
     "lfm_argmax", "lfm_argmax_noalloc", "lfm_tc_gemm_f16", "lfm_tc_gemm_f16_bmn", "lfm_attention_prefill", "lfm_selftest_wait_timeout", "lfm_q6k_prompt_gemm", "lfm_q6k_prompt_grouped",
+    "lfm_q6k_expand_f16", "lfm_q6k_prompt_gemm_x16", "lfm_q6k_prompt_grouped_x16",
     "lfm_ops_error",
     "lfm_text_create", "lfm_text_destroy", "lfm_text_push", "lfm_text_finish", "lfm_text_reset", "lfm_text_error",
 ]
@@ -113,6 +114,9 @@ def lib() -> ctypes.CDLL:
         "lfm_selftest_wait_timeout": ([ctypes.POINTER(U32), ctypes.POINTER(ctypes.c_uint64)], st),
         "lfm_q6k_prompt_gemm": ([P, U32, U32, P, U32, P, P], st),
         "lfm_q6k_prompt_grouped": ([P, U32, U32, U32, P, P, U32, U32, P, P], st),
+        "lfm_q6k_expand_f16": ([P, U32, U32, P, P], st),
+        "lfm_q6k_prompt_gemm_x16": ([P, P, U32, U32, P, U32, P, P], st),
+        "lfm_q6k_prompt_grouped_x16": ([P, P, U32, U32, U32, P, P, U32, U32, P, P], st),
         "lfm_ops_error": ([], ctypes.c_char_p),
         "lfm_text_create": ([P, P, U32, U32, ctypes.c_int, ctypes.c_int, ctypes.POINTER(P)], st),
         "lfm_text_destroy": ([P], None),

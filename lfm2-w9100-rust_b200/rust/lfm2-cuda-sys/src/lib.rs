@@ -134,6 +134,13 @@ extern "C" {
     pub fn lfm_q6k_prompt_grouped(w_dev: *const c_void, in_dim: u32, rows: u32, n_expert: u32,
                                   expert_ids_dev: *const i32, x_dev: *const f32, x_div: u32, n: u32,
                                   y_dev: *mut f32, stream: *mut c_void) -> lfm_status;
+    pub fn lfm_q6k_expand_f16(w_dev: *const c_void, in_dim: u32, rows: u32, out_dev: *mut c_void,
+                              stream: *mut c_void) -> lfm_status;
+    pub fn lfm_q6k_prompt_gemm_x16(w_dev: *const c_void, w16_dev: *const c_void, in_dim: u32, rows: u32,
+                                   x_dev: *const f32, n: u32, y_dev: *mut f32, stream: *mut c_void) -> lfm_status;
+    pub fn lfm_q6k_prompt_grouped_x16(w_dev: *const c_void, w16_dev: *const c_void, in_dim: u32, rows: u32,
+                                      n_expert: u32, expert_ids_dev: *const i32, x_dev: *const f32, x_div: u32,
+                                      n: u32, y_dev: *mut f32, stream: *mut c_void) -> lfm_status;
     pub fn lfm_selftest_wait_timeout(status: *mut u32, cycles: *mut u64) -> lfm_status;
     pub fn lfm_ops_error() -> *const c_char;
     // ---- streaming text of sessions decoded together (host only)

@@ -166,3 +166,169 @@ def test_tc_gemm_f16_mn_major_b(cuda_lib, m, k):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max() / np.abs(ref).max()
     assert err < 1e-5, err
+
+
+# ------------------------------------------------- expanded fp16 weight operand
+def _q6_ints(raw):
+    """sc * (q - 32) of every weight of Q6_K blocks (q6k.rs:74-146 without d):
+    ql[128], qh[64], int8 scales[16], fp16 d per 210-byte block."""
+    b = raw.reshape(-1, 210)
+    ql, qh = b[:, :128].astype(np.int32), b[:, 128:192].astype(np.int32)
+    sc = b[:, 192:208].view(np.int8).astype(np.int32)
+    out = np.empty((b.shape[0], 256), np.int32)
+    for h in range(2):
+        l = np.arange(32)
+        lq, hq = ql[:, 64 * h:64 * h + 64], qh[:, 32 * h:32 * h + 32]
+        q = [(lq[:, l] & 15) | ((hq[:, l] & 3) << 4), (lq[:, l + 32] & 15) | (((hq[:, l] >> 2) & 3) << 4),
+             (lq[:, l] >> 4) | (((hq[:, l] >> 4) & 3) << 4), (lq[:, l + 32] >> 4) | (((hq[:, l] >> 6) & 3) << 4)]
+        for j in range(4):
+            s = sc[:, 8 * h + 2 * j + l // 16]
+            out[:, 128 * h + 32 * j + l] = s * (q[j] - 32)
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("in_dim,rows,full", [(2048, 256, False), (1792, 128, True)])
+def test_expand_f16_exact(cuda_lib, oracle_mod, in_dim, rows, full):
+    """The expanded operand holds sc*(q-32) rounded to fp16 (exact up to 2048;
+    with full-range scales, odd products above 2048 round to even, as in the
+    on-chip path); d times the integers is the reference dequantisation to
+    within its own f32 rounding."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(in_dim + rows)
+    raw, w = _q6(cuda_lib, rng, in_dim, rows, full)
+    w16 = torch.full((rows, in_dim), float("nan"), dtype=torch.float16, device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_expand_f16(_ptr(w), in_dim, rows, _ptr(w16), None), "expand_f16")
+    torch.cuda.synchronize()
+    got = w16.cpu().numpy().astype(np.float64).reshape(-1)
+    ints = _q6_ints(raw)
+    assert np.array_equal(got, ints.astype(np.float16).astype(np.float64))
+    d = raw.reshape(-1, 210)[:, 208:210].copy().view(np.float16).astype(np.float64)
+    deq = oracle_mod.dequant_blocks(raw).astype(np.float64)
+    assert np.allclose((ints.reshape(-1, 256) * d).reshape(-1), deq, rtol=2.0 ** -23, atol=0)
+
+
+@pytest.mark.parametrize("in_dim,rows,n,full", [(2048, 2048, 100, False), (2048, 6144, 3, False),
+                                                (7168, 2048, 257, True), (2048, 512, 1000, False)])
+def test_prompt_gemm_x16_bit_identical(cuda_lib, oracle_mod, in_dim, rows, n, full):
+    """Reading the expanded operand gives the on-chip-dequantising GEMM's
+    output bit for bit (same integers, same MMAs, same fold order)."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(in_dim + 7 * rows + n)
+    raw, w = _q6(cuda_lib, rng, in_dim, rows, full)
+    w16 = torch.empty((rows, in_dim), dtype=torch.float16, device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_expand_f16(_ptr(w), in_dim, rows, _ptr(w16), None), "expand_f16")
+    x = rng.normal(0, 1, size=(n, in_dim)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    ya = torch.full((n, rows), float("nan"), device="cuda")
+    yb = torch.full((n, rows), float("nan"), device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_gemm(_ptr(w), in_dim, rows, _ptr(xd), n, _ptr(ya), None), "gemm")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_gemm_x16(_ptr(w), _ptr(w16), in_dim, rows, _ptr(xd), n, _ptr(yb),
+                                                         None), "gemm_x16")
+    a, b = ya.cpu().numpy(), yb.cpu().numpy()
+    assert np.isfinite(b).all()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    wf = oracle_mod.dequant_blocks(raw).reshape(rows, in_dim).astype(np.float64)
+    ref = x.astype(np.float64) @ wf.T
+    assert _rel(b.astype(np.float64), ref) < (TOL_FULL if full else TOL_SYNTH)
+
+
+@pytest.mark.parametrize("in_dim,rows,x_div,n", [(2048, 1792, 4, 300), (1792, 2048, 1, 77), (1792, 2048, 1, 1200)])
+def test_prompt_grouped_x16_bit_identical(cuda_lib, oracle_mod, in_dim, rows, x_div, n):
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(in_dim + n + 11 * x_div)
+    n_expert = 32
+    raw, w = _q6(cuda_lib, rng, in_dim, n_expert * rows)
+    w16 = torch.empty((n_expert * rows, in_dim), dtype=torch.float16, device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_expand_f16(_ptr(w), in_dim, n_expert * rows, _ptr(w16), None),
+                        "expand_f16")
+    ids = np.stack([rng.permutation(n_expert)[:4] for _ in range(n)]).astype(np.int32)
+    xrows = n if x_div == 4 else 4 * n
+    x = rng.normal(0, 1, size=(xrows, in_dim)).astype(np.float32)
+    idd, xd = torch.from_numpy(ids.reshape(-1)).cuda(), torch.from_numpy(x).cuda()
+    ya = torch.full((4 * n, rows), float("nan"), device="cuda")
+    yb = torch.full((4 * n, rows), float("nan"), device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, n_expert, _ptr(idd), _ptr(xd), x_div,
+                                                        n, _ptr(ya), None), "grouped")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped_x16(_ptr(w), _ptr(w16), in_dim, rows, n_expert, _ptr(idd),
+                                                            _ptr(xd), x_div, n, _ptr(yb), None), "grouped_x16")
+    a, b = ya.cpu().numpy(), yb.cpu().numpy()
+    assert np.isfinite(b).all()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_expand_rejects_bad_arguments(cuda_lib):
+    import torch
+    w = torch.zeros(128 * 8 * 210, dtype=torch.uint8, device="cuda")
+    out = torch.zeros(128 * 2048 + 8, dtype=torch.float16, device="cuda")
+    misaligned = ctypes.c_void_p(out.data_ptr() + 2)
+    assert cuda_lib.lfm_q6k_expand_f16(_ptr(w), 2048, 128, misaligned, None) != 0
+    assert cuda_lib.lfm_q6k_expand_f16(_ptr(w), 100, 128, _ptr(out), None) != 0
+    x = torch.zeros(2048, device="cuda")
+    y = torch.zeros(128, device="cuda")
+    assert cuda_lib.lfm_q6k_prompt_gemm_x16(_ptr(w), misaligned, 2048, 128, _ptr(x), 1, _ptr(y), None) != 0
+
+
+_TWO_SM_CHECK = r"""
+import ctypes, sys
+import numpy as np
+import torch
+sys.path[:0] = [sys.argv[1], sys.argv[2]]
+import lfm2_b200
+from test_gpu_kernels import random_q6
+lib = lfm2_b200.lib()
+P = lambda t: ctypes.c_void_p(t.data_ptr())
+def up(raw, in_dim, rows):
+    dev = torch.empty(raw.size, dtype=torch.uint8, device="cuda")
+    lfm2_b200.ops_check(lib.lfm_q6k_upload(raw.ctypes.data_as(ctypes.c_void_p), in_dim, rows, P(dev)), "upload")
+    return dev
+def exp16(w, in_dim, rows):
+    w16 = torch.empty((rows, in_dim), dtype=torch.float16, device="cuda")
+    lfm2_b200.ops_check(lib.lfm_q6k_expand_f16(P(w), in_dim, rows, P(w16), None), "expand")
+    return w16
+rng = np.random.default_rng(77)
+for in_dim, rows, n in [(2048, 2048, 300), (7168, 2048, 129), (2048, 6144, 1000)]:
+    w = up(random_q6(rng, rows * in_dim // 256, True), in_dim, rows)
+    w16 = exp16(w, in_dim, rows)
+    x = torch.from_numpy(rng.normal(0, 1, size=(n, in_dim)).astype(np.float32)).cuda()
+    ya = torch.full((n, rows), float("nan"), device="cuda")
+    yb = torch.full((n, rows), float("nan"), device="cuda")
+    lfm2_b200.ops_check(lib.lfm_q6k_prompt_gemm(P(w), in_dim, rows, P(x), n, P(ya), None), "gemm")
+    lfm2_b200.ops_check(lib.lfm_q6k_prompt_gemm_x16(P(w), P(w16), in_dim, rows, P(x), n, P(yb), None), "gemm_x16")
+    assert torch.isfinite(yb).all()
+    assert torch.equal(ya.view(torch.int32), yb.view(torch.int32)), (in_dim, rows, n)
+for in_dim, rows, x_div, n in [(1792, 2048, 1, 1200), (2048, 1792, 4, 1500)]:
+    w = up(random_q6(rng, 32 * rows * in_dim // 256), in_dim, 32 * rows)
+    w16 = exp16(w, in_dim, 32 * rows)
+    ids = torch.from_numpy(np.stack([rng.permutation(32)[:4] for _ in range(n)]).astype(np.int32).ravel()).cuda()
+    x = torch.from_numpy(rng.normal(0, 1, size=((n if x_div == 4 else 4 * n), in_dim)).astype(np.float32)).cuda()
+    ya = torch.full((4 * n, rows), float("nan"), device="cuda")
+    yb = torch.full((4 * n, rows), float("nan"), device="cuda")
+    lfm2_b200.ops_check(lib.lfm_q6k_prompt_grouped(P(w), in_dim, rows, 32, P(ids), P(x), x_div, n, P(ya), None), "g")
+    lfm2_b200.ops_check(lib.lfm_q6k_prompt_grouped_x16(P(w), P(w16), in_dim, rows, 32, P(ids), P(x), x_div, n,
+                                                       P(yb), None), "g_x16")
+    assert torch.isfinite(yb).all()
+    assert torch.equal(ya.view(torch.int32), yb.view(torch.int32)), (in_dim, rows, n)
+print("OK")
+"""
+
+
+def test_two_sm_gemm_bit_identical():
+    """The 2-SM (cta_group::2, M=256) form of the expanded-weight GEMM, which
+    serves 128-token tiles when LFM_PREFILL_2SM=1, gives the 1-SM results bit
+    for bit (dense and grouped; run in a child process because the switch is
+    read once per process)."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    pkg = os.path.join(os.path.dirname(here), "lfm2-w9100-rust_b200")
+    env = dict(os.environ, LFM_PREFILL_2SM="1")
+    r = subprocess.run([sys.executable, "-c", _TWO_SM_CHECK, here, pkg], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout[-2000:] + r.stderr[-2000:]
