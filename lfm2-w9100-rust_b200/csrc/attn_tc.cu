@@ -12,11 +12,15 @@
 //   warp 1     TMEM (512 columns) and the MMAs:
 //              S = Qhi K^T + Qlo K^T      (M=128, N=128, two S buffers)
 //              O_t = Phi V + Plo V       (M=128, N=64, V MN-major, two buffers)
-//   warps 2-5  one row per thread: q -> fp16 hi/lo operand (scaled by 1/8);
-//              per tile two passes over the S row in TMEM (max, then
-//              p = exp(s - m) written as an fp16 hi/lo pair, the A operand
-//              of P.V); the running output O (64 registers) is rescaled and
-//              added to the previous tile's O_t (online softmax).
+//   warps 2-9  softmax: each row is shared by two warps of the same TMEM lane
+//              quarter, one per half of the S tile's 64-column halves (and
+//              of the output's 32-column halves): q -> fp16 hi/lo operand
+//              (scaled by 1/8); per tile two passes over the thread's 64 S
+//              values in TMEM (max, combined with the partner warp through
+//              shared memory; then p = exp(s - m) written as an fp16 hi/lo
+//              pair, the A operand of P.V, into one of two P buffers); the
+//              running output (32 registers) is rescaled and added to the
+//              previous tile's O_t (online softmax).
 // The hi/lo pairs carry about 22 significant bits of q and p, the K/V cache
 // values are exact in fp16, and every product accumulates in fp32, so the
 // result matches the fp32 formulation to a few units of 2^-22.
@@ -42,13 +46,16 @@ using namespace tc;
 
 constexpr int AQ = 32;                  // query tokens per CTA (x 4 heads = 128 rows)
 constexpr int KT = 128;                 // key positions per tile
-constexpr int ATHREADS = 6 * 32;
+constexpr int ATHREADS = 10 * 32;
+constexpr int NSOFT = 8;                // softmax warps
 constexpr int Q_BYTES = 128 * 128;      // 128 rows x 64 fp16
 constexpr int KV_BYTES = KT * 128;      // 128 positions x 64 fp16
 constexpr int P_BYTES = 128 * 256;      // 128 rows x 128 fp16 (two 64-wide chunks)
+// P buffer b: hi rows at OFF_P + 2 b P_BYTES, lo rows P_BYTES after them
 constexpr int OFF_QH = 0, OFF_QL = Q_BYTES, OFF_K = 2 * Q_BYTES, OFF_V = OFF_K + 2 * KV_BYTES,
-              OFF_PH = OFF_V + 2 * KV_BYTES, OFF_PL = OFF_PH + P_BYTES;
-constexpr int ASMEM = OFF_PL + P_BYTES + 1024;
+              OFF_P = OFF_V + 2 * KV_BYTES;
+constexpr int ASMEM = OFF_P + 4 * P_BYTES + 1024;
+static_assert(ASMEM + 2048 <= 232448, "attention shared memory");
 constexpr uint32_t ATMEM_COLS = 512;    // S: [0, 256), O_t: [256, 384)
 constexpr uint32_t IDESC_S = idesc_f16(128, KT, false);
 constexpr uint32_t IDESC_PV = idesc_f16(128, HEAD_DIM, true);
@@ -83,13 +90,19 @@ __device__ __forceinline__ void split8(const float (&f)[8], uint4& hi, uint4& lo
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// the two softmax warps of a row quarter meet on named barrier 1 + quarter
+__device__ __forceinline__ void pair_sync(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
+
 __global__ void __launch_bounds__(ATHREADS, 1)
     k_attn_tc(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV, AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full[2],
+  __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full[2],
       o_empty[2], mma_done;
   __shared__ uint32_t tmem_base;
+  __shared__ float s_red[2][128];  // per row: the two halves' maxima, at the end their sums
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = (p.n + AQ - 1) / AQ;
   const int kh = blockIdx.x;
@@ -99,17 +112,17 @@ __global__ void __launch_bounds__(ATHREADS, 1)
   const int ntiles = (p.start + last_tok) / KT + 1;
 
   if (threadIdx.x == 0) {
-    mbar_init(&q_full, 4);
+    mbar_init(&q_full, NSOFT);
     for (int b = 0; b < 2; b++) {
       mbar_init(&kv_full[b], 1);
       mbar_init(&kv_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4);
+      mbar_init(&s_empty[b], NSOFT);
       mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 4);
+      mbar_init(&o_empty[b], NSOFT);
+      mbar_init(&p_full[b], NSOFT);
+      mbar_init(&p_empty[b], 1);
     }
-    mbar_init(&p_full, 4);
-    mbar_init(&p_empty, 1);
     mbar_init(&mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -137,7 +150,6 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     if (lane == 0) {
       // -------------------------------------------------------------- MMA
       const uint32_t qh = smem_u32(smem + OFF_QH), ql = smem_u32(smem + OFF_QL);
-      const uint32_t ph = smem_u32(smem + OFF_PH), pl = smem_u32(smem + OFF_PL);
       bool ok = mbar_wait(&q_full, 0, p.err);
       auto issue_s = [&](int i) -> bool {
         const int b = i & 1;
@@ -159,9 +171,10 @@ __global__ void __launch_bounds__(ATHREADS, 1)
       for (int i = 0; i < ntiles && ok; i++) {
         if (i + 1 < ntiles && !(ok = issue_s(i + 1))) break;
         const int b = i & 1;
-        if (!(ok = mbar_wait(&p_full, i & 1, p.err))) break;
+        if (!(ok = mbar_wait(&p_full[b], (i >> 1) & 1, p.err))) break;
         if (i >= 2 && !(ok = mbar_wait(&o_empty[b], ((i >> 1) - 1) & 1, p.err))) break;
         tc_fence_after();
+        const uint32_t ph = smem_u32(smem + OFF_P + b * 2 * P_BYTES), pl = ph + P_BYTES;
         const uint32_t d = tmem + 256u + (uint32_t)(b * HEAD_DIM);
         const uint32_t vb = smem_u32(smem + OFF_V + b * KV_BYTES);
 #pragma unroll
@@ -173,7 +186,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
           mma_f16(d, smem_desc_sw128(pl + (ks >> 2) * 16384 + (ks & 3) * 32), smem_desc_mn_sw128(vb + ks * 2048),
                   IDESC_PV, 1u);
         mma_commit(&o_full[b]);
-        mma_commit(&p_empty);
+        mma_commit(&p_empty[b]);
         mma_commit(&kv_empty[b]);
       }
       // tensor memory and the operand buffers stay in use until every issued MMA has finished
@@ -182,7 +195,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax rows
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;        // TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;    // S / P columns [64 half, 64 half + 64), O columns [32 half, +32)
     const int r = quarter * 32 + lane;
     const int h = kh * 4 + quarter;
     const int j = j0 + lane;
@@ -191,7 +205,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     {
       const float* qr = p.q + (size_t)(valid ? j : 0) * p.q_stride + h * HEAD_DIM;
 #pragma unroll
-      for (int pc = 0; pc < 8; pc++) {
+      for (int pc = 4 * half; pc < 4 * half + 4; pc++) {
         float f[8];
         const float4 a = valid ? *(const float4*)(qr + 8 * pc) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 b = valid ? *(const float4*)(qr + 8 * pc + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -206,56 +220,64 @@ __global__ void __launch_bounds__(ATHREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&q_full);
     }
-    float o[HEAD_DIM];
+    float o[HEAD_DIM / 2];
 #pragma unroll
-    for (int d = 0; d < HEAD_DIM; d++) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    for (int d = 0; d < HEAD_DIM / 2; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;  // l: this half's share of the row sum
     bool ok = true;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    for (int i = 0; i < ntiles && ok; i++) {
+    for (int i = 0; i < ntiles; i++) {
       const int b = i & 1;
-      if (!(ok = mbar_wait(&s_full[b], (i >> 1) & 1, p.err))) break;
+      // every softmax warp walks every tile (also after a wait gave up) so
+      // that the pair barriers always meet
+      if (ok) ok = mbar_wait(&s_full[b], (i >> 1) & 1, p.err);
       tc_fence_after();
-      const uint32_t sbase = lane_base + (uint32_t)(b * KT);
-      const int tile0 = i * KT;
-      const bool need_mask = tile0 + KT - 1 > pr;
-      // pass 1: row maximum over the visible positions
+      const uint32_t sbase = lane_base + (uint32_t)(b * KT + 64 * half);
+      const int col0 = i * KT + 64 * half;  // key position of this thread's first column
+      const bool need_mask = col0 + 63 > pr;
+      // pass 1: maximum over this half's visible positions, then over the row
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < KT / 32; c++) {
-        uint32_t v[32];
-        tmem_ld32(sbase + 32 * c, v);
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[16];
+        tmem_ld16_nowait(sbase + 16 * c, v);
+        tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
+        for (int e = 0; e < 16; e++) {
           const float s = __uint_as_float(v[e]);
-          mx = fmaxf(mx, (!need_mask || tile0 + 32 * c + e <= pr) ? s : -INFINITY);
+          mx = fmaxf(mx, (!need_mask || col0 + 16 * c + e <= pr) ? s : -INFINITY);
         }
       }
-      const float m_new = fmaxf(m, mx);  // finite: position 0 is visible to every row
+      s_red[half][r] = mx;
+      pair_sync(quarter);
+      const float m_new = fmaxf(m, fmaxf(s_red[0][r], s_red[1][r]));  // finite: position 0 is visible to every row
+      pair_sync(quarter);  // both reads done before the next tile's writes
       const float alpha = exp2f((m - m_new) * LOG2E);
-      // pass 2: probabilities -> fp16 hi/lo operand (after the previous P.V has read it)
-      if (i >= 1 && !(ok = mbar_wait(&p_empty, (i - 1) & 1, p.err))) break;
+      // pass 2: probabilities -> fp16 hi/lo operand in P buffer b (after the
+      // P.V of tile i - 2 has read it)
+      if (ok && i >= 2) ok = mbar_wait(&p_empty[b], ((i >> 1) - 1) & 1, p.err);
+      uint8_t* pbuf = smem + OFF_P + b * 2 * P_BYTES + half * 16384;
       const float mlog = m_new * LOG2E;
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < KT / 32; c++) {
-        uint32_t v[32];
-        tmem_ld32(sbase + 32 * c, v);
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[16];
+        tmem_ld16_nowait(sbase + 16 * c, v);
+        tmem_wait_ld();
 #pragma unroll
-        for (int g = 0; g < 4; g++) {
+        for (int g = 0; g < 2; g++) {
           float f[8];
 #pragma unroll
           for (int e = 0; e < 8; e++) {
-            const int col = 32 * c + 8 * g + e;
+            const int col = col0 + 16 * c + 8 * g + e;
             const float pe = exp2f(fmaf(__uint_as_float(v[8 * g + e]), LOG2E, -mlog));
-            f[e] = (!need_mask || tile0 + col <= pr) ? pe : 0.f;
+            f[e] = (!need_mask || col <= pr) ? pe : 0.f;
             sum += f[e];
           }
           uint4 hi, lo;
           split8(f, hi, lo);
-          const int col = 32 * c + 8 * g;
-          st_piece(smem + OFF_PH + (col >> 6) * 16384, r, (col & 63) >> 3, hi);
-          st_piece(smem + OFF_PL + (col >> 6) * 16384, r, (col & 63) >> 3, lo);
+          st_piece(pbuf, r, 2 * c + g, hi);
+          st_piece(pbuf + P_BYTES, r, 2 * c + g, lo);
         }
       }
       tc_fence_before();
@@ -263,46 +285,43 @@ __global__ void __launch_bounds__(ATHREADS, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s_empty[b]);
-        mbar_arrive(&p_full);
+        mbar_arrive(&p_full[b]);
       }
       l = l * alpha + sum;
       m = m_new;
       // fold the previous tile's P.V into the running output
       if (i >= 1) {
         const int pb = (i - 1) & 1;
-        if (!(ok = mbar_wait(&o_full[pb], ((i - 1) >> 1) & 1, p.err))) break;
+        if (ok) ok = mbar_wait(&o_full[pb], ((i - 1) >> 1) & 1, p.err);
         tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(lane_base + 256u + (uint32_t)(pb * HEAD_DIM + 32 * half), v);
 #pragma unroll
-        for (int c = 0; c < HEAD_DIM / 32; c++) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + 256u + (uint32_t)(pb * HEAD_DIM + 32 * c), v);
-#pragma unroll
-          for (int e = 0; e < 32; e++) o[32 * c + e] = fmaf(o[32 * c + e], alpha_prev, __uint_as_float(v[e]));
-        }
+        for (int e = 0; e < 32; e++) o[e] = fmaf(o[e], alpha_prev, __uint_as_float(v[e]));
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_empty[pb]);
       }
       alpha_prev = alpha;
     }
-    if (ok) {
-      const int pb = (ntiles - 1) & 1;
-      ok = mbar_wait(&o_full[pb], ((ntiles - 1) >> 1) & 1, p.err);
-      tc_fence_after();
+    const int pb = (ntiles - 1) & 1;
+    if (ok) ok = mbar_wait(&o_full[pb], ((ntiles - 1) >> 1) & 1, p.err);
+    tc_fence_after();
+    {
+      uint32_t v[32];
+      tmem_ld32(lane_base + 256u + (uint32_t)(pb * HEAD_DIM + 32 * half), v);
 #pragma unroll
-      for (int c = 0; c < HEAD_DIM / 32; c++) {
-        uint32_t v[32];
-        tmem_ld32(lane_base + 256u + (uint32_t)(pb * HEAD_DIM + 32 * c), v);
+      for (int e = 0; e < 32; e++) o[e] = fmaf(o[e], alpha_prev, __uint_as_float(v[e]));
+    }
+    s_red[half][r] = l;
+    pair_sync(quarter);
+    const float lsum = s_red[0][r] + s_red[1][r];
+    if (ok && valid) {
+      const float inv = 1.0f / lsum;
+      float* dst = p.out + (size_t)j * p.out_stride + h * HEAD_DIM + 32 * half;
 #pragma unroll
-        for (int e = 0; e < 32; e++) o[32 * c + e] = fmaf(o[32 * c + e], alpha_prev, __uint_as_float(v[e]));
-      }
-      if (ok && valid) {
-        const float inv = 1.0f / l;
-        float* dst = p.out + (size_t)j * p.out_stride + h * HEAD_DIM;
-#pragma unroll
-        for (int d = 0; d < HEAD_DIM; d += 4)
-          *(float4*)(dst + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-      }
+      for (int d = 0; d < 32; d += 4)
+        *(float4*)(dst + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
     }
   }
   tc_fence_before();
