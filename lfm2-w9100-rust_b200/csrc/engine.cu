@@ -653,6 +653,10 @@ void EngineImpl::build_step() {
       step_reason = "persistent step unavailable: too few SMs for the per-CTA partial buffer";
       return;
     }
+    if (q.type == ST_XSWIGLU && q.ntiles / sms < STEP_PRODUCERS) {
+      step_reason = "persistent step unavailable: more SMs than the routed stages have tiles for every producer";
+      return;
+    }
   }
   if ((int)st.size() > STEP_MAX_STAGES || embd.rows % 16 != 0) {
     step_reason = "persistent step unavailable: model shape outside the step kernel's tiling";

@@ -7,15 +7,20 @@
 // (monotonic arrival counters in global memory, acquire/release ordering,
 // bounded polling).
 //
-// Warp 16 (the last) of each CTA is a dedicated producer: it walks this CTA's
-// weight tiles of ALL stages in order and streams them through a 4-slot
-// shared-memory ring with bulk async copies (cp.async.bulk into this CTA only)
-// completed on mbarriers. It waits only for free ring slots and, before
-// routed-expert tiles, for the layer's top-4 experts, which the consumers
-// compute at the start of the gate/up stage from the router partials the
-// residual stage publishes (there is no router stage). The weight stream of
-// later stages is in flight while earlier stages compute and the grid
-// barriers never drain the HBM pipeline.
+// Warps 16-19 of each CTA are producers: together they walk this CTA's weight
+// tiles of ALL stages in order and stream them through a 4-slot shared-memory
+// ring with bulk async copies (cp.async.bulk into this CTA only) completed on
+// mbarriers; producer p issues the tiles that land in slot p. A producer
+// waits only for its free slot and, before routed-expert tiles, for the
+// layer's top-4 experts, which the consumers compute at the start of the
+// gate/up stage from the router partials the residual stage publishes (there
+// is no router stage). The weight stream of later stages is in flight while
+// earlier stages compute and the grid barriers never drain the HBM pipeline.
+// One producer per slot, not one for all: issuing a bulk copy whose source
+// page misses the address-translation caches holds the issuing thread for
+// several hundred cycles, and a decode tile is six copies from six different
+// weight pages, so a single issuing thread held the stream near 2 TB/s;
+// four issuers overlap those stalls.
 //
 // Warps 0-15 consume. Each holds the stage's activation unit in registers (one
 // 64-weight unit per lane, q6k.cuh layout) and computes one dot row of every
@@ -43,11 +48,13 @@ namespace {
 using namespace dev;
 
 constexpr int NCW = 16;                // consumer warps
-constexpr int NT = (NCW + 1) * 32;     // + the producer warp
+constexpr int NPROD = STEP_PRODUCERS;  // producer warps, one per ring slot
+constexpr int NT = (NCW + NPROD) * 32;  // 20 warps x 96 registers fit one SM
 constexpr int MAXREG = 96;             // 17 warps: 5 on one SM sub-partition x 96 registers
 constexpr int PART_TILES = STEP_PART_TILES;
-constexpr int PRODUCER = NCW;          // warp index of the producer
+constexpr int PRODUCER = NCW;          // warp index of the first producer
 constexpr int RING = 4;
+static_assert(NPROD == RING, "one producer warp per ring slot");
 constexpr int SLOT = 40320;            // 24 rows x (1536 + 128 + 16): the largest tile
 constexpr int KP = HEAD_DIM + 8;       // padded fp16 K row in shared memory
 // 32-position chunks per attention task: at most 32 tasks per kv head, so a
@@ -350,14 +357,22 @@ __device__ float route_layer(const StepParams& P, const float* bias, ConsShared&
   return buf[G * W + N_EXPERT];
 }
 
-// The producer warp: all ring tiles of this CTA, in stage order (lane 0
-// issues, the warp computes each MoE layer's routing). Returns the number of
-// tiles issued; on abort it stops early.
+// Producer warp p: walks all ring tiles of this CTA in stage order and issues
+// those that land in ring slot p (global tile index k with k % RING == p;
+// lane 0 issues). Returns the global index of the last tile it issued (-1
+// if none); on abort it stops early.
+//
+// Every producer waits for each MoE layer's routing (one phase of
+// cs.route_bar per layer, observed by parity). That stays in step because
+// every producer has a tile in every routed gate/up stage (at least RING
+// consecutive tiles per CTA, checked when the stage list is built), so the
+// consumers cannot publish the next layer's routing before each producer has
+// passed this one.
 __device__ int producer(const StepParams& P, const StepStage* stg, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                        unsigned target, ConsShared& cs) {
+                        ConsShared& cs, int p) {
   StepCtl* ctl = P.ctl;
   const int lane = threadIdx.x & 31;
-  int k = 0;
+  int k = 0, last = -1;
   int sel[N_USED] = {0, 0, 0, 0};
   int routed = -1;  // residual stage whose routing `sel` holds
   uint32_t rphase = 0;
@@ -370,7 +385,7 @@ __device__ int producer(const StepParams& P, const StepStage* stg, uint8_t* ring
       // stage and release cs.route_bar (one phase per MoE layer)
       int ok = 1;
       if (lane == 0) ok = ring_wait(&cs.route_bar, rphase, ctl) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return k;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return last;
 #pragma unroll
       for (int i = 0; i < N_USED; i++) sel[i] = cs.psel[i];
       rphase ^= 1u;
@@ -380,14 +395,16 @@ __device__ int producer(const StepParams& P, const StepStage* stg, uint8_t* ring
     tile_range(S.ntiles, t0, t1);
     for (int t = t0; t < t1; t++, k++) {
       const int st = k % RING, round = k / RING;
+      if (st != p) continue;
       int ok = 1;
       if (lane == 0 && round > 0) ok = ring_wait(&empty[st], (round - 1) & 1, ctl) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return k;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return last;
       if (lane == 0) issue_tile(S, sel, t, ring + st * SLOT, &full[st]);
+      last = k;
       __syncwarp();
     }
   }
-  return k;
+  return last;
 }
 
 // ------------------------------------------------------------- consumers
@@ -863,13 +880,12 @@ __global__ void __maxnreg__(MAXREG) k_step(StepParams P) {
   }
   __syncthreads();
 
-  if (warp == PRODUCER) {
-    const int issued = producer(P, stg, ring, full, empty, target, cs);
+  if (warp >= PRODUCER) {
+    const int last = producer(P, stg, ring, full, empty, cs, warp - PRODUCER);
     // every issued copy must land before the CTA may exit (bounded waits,
-    // regardless of the abort flag)
-    if (lane == 0)
-      for (int j = issued > RING ? issued - RING : 0; j < issued; j++)
-        mbar_wait(&full[j % RING], (j / RING) & 1, nullptr);
+    // regardless of the abort flag): the slot's earlier tiles were consumed
+    // before it was reused, so only the last one can be in flight
+    if (lane == 0 && last >= 0) mbar_wait(&full[last % RING], (last / RING) & 1, nullptr);
     return;
   }
 

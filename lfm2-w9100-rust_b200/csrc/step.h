@@ -47,6 +47,9 @@ struct StepStage {
 
 constexpr int STEP_MAX_STAGES = 192;
 constexpr int STEP_MAX_CTAS = 160;
+// producer warps of the step kernel (one per weight-ring slot); every CTA
+// needs at least this many tiles in each routed gate/up stage
+constexpr int STEP_PRODUCERS = 4;
 // Most tiles one CTA may own in a stage whose rows are finished at stage end
 // (short conv, SwiGLU, expert and dense down projections).
 constexpr int STEP_PART_TILES = 16;
