@@ -50,7 +50,7 @@ using namespace dev;
 constexpr int NCW = 16;                // consumer warps
 constexpr int NPROD = STEP_PRODUCERS;  // producer warps, one per ring slot
 constexpr int NT = (NCW + NPROD) * 32;  // 20 warps x 96 registers fit one SM
-constexpr int MAXREG = 96;             // 17 warps: 5 on one SM sub-partition x 96 registers
+constexpr int MAXREG = 96;             // 20 warps: 5 per SM sub-partition x 32 lanes x 96 registers
 constexpr int PART_TILES = STEP_PART_TILES;
 constexpr int PRODUCER = NCW;          // warp index of the first producer
 constexpr int RING = 4;
@@ -479,7 +479,7 @@ __device__ __forceinline__ void stage_x(const StepParams& P, const StepStage& S,
 //   XDOWN                : 4 experts x 4 output rows, row w (expert w/4)
 //   DOWN28               : 4 rows x 7168 = 4 quarters of 28 units; quarter w%4 of row w/4
 // Not inlined: one kernel body holding all eight instantiations needs more
-// registers than a thread has with 17 warps per SM; as separate functions
+// registers than a thread has with 20 warps per SM; as separate functions
 // each tile loop is allocated on its own.
 template <int TYPE>
 __device__ __noinline__ bool ring_stage(const StepParams& P, const StepStage& S, int sidx, uint8_t* ring,
