@@ -632,11 +632,11 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
 // its activation chunks and no warp dequantises. Same MMAs, same
 // per-super-block TMEM accumulators, same fold y += d * (hi + lo) and the same
 // stores, so the results are bit-identical to k_tc_q6's.
-//   warp 0        TMA: lane 0 the activation chunks (as k_tc_q6), lane 1 the
-//                 A chunks (64-wide K x 128 rows, 128-byte swizzle)
+//   warp 0        TMA: the activation chunks (as k_tc_q6)
 //   warp 1        TMEM allocation and the MMA issue (as k_tc_q6)
 //   warps 2-9     fold each super-block's accumulator as soon as it is complete,
 //                 then store
+//   warp 10       TMA: the A chunks (64-wide K x 128 rows, 128-byte swizzle)
 #ifndef LFM_X_A128
 #define LFM_X_A128 4
 #endif
@@ -655,8 +655,15 @@ static_assert(x_smem(128) <= 232448 - 2048 && x_smem(64) <= 232448 - 2048 && x_s
                   x_smem(16) <= 110 * 1024,
               "expanded-weight GEMM shared memory");
 
+// warps of k_tc_q6x: 0 activation loads, 1 MMA, 2-9 fold and store, 10 weight
+// loads. Each TMA load holds its issuing thread for a few hundred cycles and
+// the lanes of one warp issue one after another, so the two operand streams
+// have a warp each.
+constexpr int XTHREADS = 11 * 32;
+constexpr int XA_WARP = 10;
+
 template <int TT>
-__global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
+__global__ void __launch_bounds__(XTHREADS, q_ctas_per_sm(TT))
     k_tc_q6x(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
   constexpr int QB_BYTES = 2 * TT * 128;
   constexpr uint32_t QTMEM_COLS = q_tmem_cols(TT);
@@ -718,10 +725,10 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 0) {
-    if (lane == 0 || lane == 1) {
-      // lane 0: activation chunks (hi and lo rows); lane 1: A chunks
-      const bool act = lane == 0;
+  if (warp == 0 || warp == XA_WARP) {
+    if (lane == 0) {
+      // warp 0: activation chunks (hi and lo rows); warp XA_WARP: A chunks
+      const bool act = warp == 0;
       const int NS = act ? BSTAGES : ASTAGES;
       uint64_t* full = act ? bfull : afull;
       uint64_t* empty = act ? bempty : aempty;
@@ -781,7 +788,7 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0, nullptr);
     }
-  } else {
+  } else if (warp < XA_WARP) {
     // --------------------------------------------------------------- workers
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
@@ -1514,7 +1521,7 @@ cudaError_t launch_q6x_tt(const CUtensorMap& ma, const CUtensorMap& mx, dim3 gri
   static std::mutex mu;
   once_per_device(done, mu,
                   [] { cudaFuncSetAttribute(k_tc_q6x<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, x_smem(TT)); });
-  k_tc_q6x<TT><<<grid, QTHREADS, x_smem(TT), s>>>(ma, mx, p);
+  k_tc_q6x<TT><<<grid, XTHREADS, x_smem(TT), s>>>(ma, mx, p);
   return cudaGetLastError();
 }
 
