@@ -485,6 +485,7 @@ def multi_session(eng, peaks, pg, ws: int, info: dict) -> dict:
             "decode_ms_per_step": round(dec_max / SESSION_GEN, 3),
             "prefill_tok_s": round(ws * float(lens.sum()) / (pf_max / 1000.0), 1),
             "e2e_tok_s": round(gen / wall_all, 1), "e2e_decode_tok_s": round(gen / wall_dec, 1),
+            "prefill_wall_s": round(reduce_max(pg, w1 - w0), 4), "prefill_device_s": round(pf_max / 1000.0, 4),
             "text_stream": dict(text, vs_decode=round(text["tok_s"] / (gen / (dec_max / 1000.0)), 1)),
             "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
                          "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
