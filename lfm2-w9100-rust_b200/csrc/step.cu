@@ -274,6 +274,9 @@ struct ConsShared {
 // 1/rms of both the router and the FFN input).
 __device__ float route_layer(const StepParams& P, const float* bias, ConsShared& cs, float* buf) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the expert bias is read long before the selection needs it (a global
+  // load issued at the selection put its latency on the routing's path)
+  const float bias_l = warp == 0 ? __ldg(bias + lane) : 0.f;
   const StepCtl* ctl = P.ctl;
   const int G = gridDim.x;
   constexpr int W = N_EXPERT + 1;
@@ -322,7 +325,7 @@ __device__ float route_layer(const StepParams& P, const float* bias, ConsShared&
     // rank of this expert among the 32 (higher score first, lower index first
     // among equal scores; a NaN score ranks last): the same order as picking
     // the maximum four times, in one round of independent shuffles
-    const float s0 = prob + bias[lane];
+    const float s0 = prob + bias_l;
     const float score = s0 == s0 ? s0 : -INFINITY;
     int rank = 0;
 #pragma unroll
