@@ -402,8 +402,7 @@ __global__ void __launch_bounds__(QTHREADS, q_ctas_per_sm(TT))
         if (round > 0 && !(ok = mbar_wait(&bempty[s], (round - 1) & 1, p.err))) break;
         uint8_t* bs = smem + OFF_B + s * QB_BYTES;
         mbar_expect_tx(&bfull[s], QB_BYTES);
-        tma_load_2d(bs, &mapX, 64 * (4 * kb0 + j), brow0, &bfull[s]);
-        tma_load_2d(bs + QB_BYTES / 2, &mapX, 64 * (4 * kb0 + j), p.rpad + brow0, &bfull[s]);
+        tma_load_3d(bs, &mapX, 64 * (4 * kb0 + j), brow0, 0, &bfull[s]);  // hi and lo rows
         issued = j + 1;
       }
       // every issued copy must land before the CTA may exit
@@ -744,8 +743,7 @@ __global__ void __launch_bounds__(XTHREADS, q_ctas_per_sm(TT))
           if (act) {
             uint8_t* bs = smem + OFF_B + s * QB_BYTES;
             mbar_expect_tx(&full[s], QB_BYTES);
-            tma_load_2d(bs, &mapX, kx, brow0, &full[s]);
-            tma_load_2d(bs + QB_BYTES / 2, &mapX, kx, p.rpad + brow0, &full[s]);
+            tma_load_3d(bs, &mapX, kx, brow0, 0, &full[s]);  // hi and lo rows
           } else {
             mbar_expect_tx(&full[s], QA_BYTES);
             tma_load_2d(smem + s * QA_BYTES, &mapA, kx, wrow0 + o0, &full[s]);
@@ -1428,6 +1426,25 @@ cudaError_t tc_map_f16(CUtensorMap* map, const void* base, int rows, int K, int 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// The hi/lo activation operand (hi rows [0, rpad), lo rows [rpad, 2 rpad), K
+// fp16 each) as a 3-D map (K, row, hi|lo) whose (64 x box_rows x 2) box brings a
+// chunk's hi rows and lo rows in one load, laid out in shared memory exactly as
+// two 2-D loads would (hi rows, then lo rows; box_rows a multiple of 8 keeps
+// the 128-byte swizzle pattern of the lo half the same).
+cudaError_t tc_map_hilo(CUtensorMap* map, const void* base, int rpad, int K, int box_rows) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (((uintptr_t)base & 15) || (K * 2) % 16 || box_rows % 8) return cudaErrorInvalidValue;
+  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rpad, 2};
+  const cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)rpad * K * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)TK, (cuuint32_t)box_rows, 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t tc_gemm_f16(const __half* A, const __half* B, int M, int N, int K, float* C, unsigned* err,
                         cudaStream_t s) {
   if (M % TM || N % TN || K % TK || K <= 0) return cudaErrorInvalidValue;
@@ -1601,7 +1618,7 @@ cudaError_t launch_q6(const Q6Mat& W, int rpad, int tt, int ntiles_y, const TcQ6
     CUtensorMap ma, mx;
     cudaError_t e = tc_map_f16(&ma, x16, W.rows, W.nb * QK, 128);
     if (e != cudaSuccess) return e;
-    e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, tt);
+    e = tc_map_hilo(&mx, sc.xg, rpad, W.nb * QK, tt);
     if (e != cudaSuccess) return e;
     // persistent: at most one wave of CTAs walks every tile
     TcQ6Params q = p;
@@ -1622,7 +1639,7 @@ cudaError_t launch_q6(const Q6Mat& W, int rpad, int tt, int ntiles_y, const TcQ6
   CUtensorMap mq, ms, mx;
   cudaError_t e = map_raw(&mq, &ms, W);
   if (e != cudaSuccess) return e;
-  e = tc_map_f16(&mx, sc.xg, 2 * rpad, W.nb * QK, tt);
+  e = tc_map_hilo(&mx, sc.xg, rpad, W.nb * QK, tt);
   if (e != cudaSuccess) return e;
   const dim3 grid(p.out_rows / 128, ntiles_y, p.ksplit);
   switch (tt) {
