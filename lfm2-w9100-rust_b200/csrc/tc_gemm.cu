@@ -952,7 +952,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-__global__ void __launch_bounds__(QTHREADS, 1)
+__global__ void __launch_bounds__(XTHREADS, 1)
     k_tc_q6x2(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapX, TcQ6Params p) {
   constexpr int TT = 128, TH = TT / 2;
   constexpr uint32_t IDESC2 = idesc_f16(256, 2 * TT, false);
@@ -1016,10 +1016,10 @@ __global__ void __launch_bounds__(QTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 0) {
-    if (lane == 0 || lane == 1) {
-      // lane 0: this CTA's half of the activation chunk; lane 1: its A chunk
-      const bool act = lane == 0;
+  if (warp == 0 || warp == XA_WARP) {
+    if (lane == 0) {
+      // warp 0: this CTA's half of the activation chunk; warp XA_WARP: its A chunk
+      const bool act = warp == 0;
       const int NS = act ? X2_BSTAGES : X2_ASTAGES;
       uint64_t* full = act ? bfull : afull;
       uint64_t* empty = act ? bempty : aempty;
@@ -1082,7 +1082,7 @@ __global__ void __launch_bounds__(QTHREADS, 1)
       // both CTAs: the leader's MMAs (which read this CTA's operands) are done
       mbar_wait(&mma_done, 0, nullptr);
     }
-  } else {
+  } else if (warp < XA_WARP) {
     // --------------------------------------------------------------- workers
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
@@ -1560,7 +1560,7 @@ int x2_max_pairs() {
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(QTHREADS, 1, 1);
+    cfg.blockDim = dim3(XTHREADS, 1, 1);
     cfg.dynamicSmemBytes = X2_SMEM;
     cfg.attrs = at;
     cfg.numAttrs = 1;
@@ -1573,8 +1573,9 @@ int x2_max_pairs() {
 }
 
 // LFM_PREFILL_2SM=1 moves 128-token tiles to the 2-SM kernel. Off by default:
-// measured on the prompt path it is bit-identical and no faster (3840 tokens
-// 32.5 vs 32.0 ms, 1024 tokens 12.1 vs 11.5 ms).
+// measured on the prompt path it is bit-identical and slower (3840 tokens
+// 31.4-31.9 vs 29.8-30.5 ms, 1024 tokens 12.1 vs 11.2 ms, both kernels with
+// their weight loads in a warp of their own).
 bool x2_enabled() {
   static const bool on = [] {
     const char* v = getenv("LFM_PREFILL_2SM");
@@ -1591,7 +1592,7 @@ cudaError_t launch_q6x2(const CUtensorMap& ma, const CUtensorMap& mx, int pairs,
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(QTHREADS, 1, 1);
+  cfg.blockDim = dim3(XTHREADS, 1, 1);
   cfg.dynamicSmemBytes = X2_SMEM;
   cfg.stream = s;
   cfg.attrs = at;
