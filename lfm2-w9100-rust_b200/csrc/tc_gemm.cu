@@ -1206,12 +1206,12 @@ __global__ void k_q6_expand_f16(Q6Mat W, __half* out) {
 // Operand rows that no block writes (tile padding) feed only output columns
 // that are never stored.
 __global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* up, int ldx, int K, int x_div,
-                                                  const int* rowof, int rpad, __half* xg, float* inv) {
+                                                  const int* rowof, int rpad, __half* xg, float* inv, int per) {
+  // slots [i0, i0 + per) share one source row (per == x_div or 1): it is read,
+  // its scale found and its hi/lo pair computed once, then written per slot
   extern __shared__ float4 srow[];  // the row (K floats)
-  const int i = blockIdx.x;
-  const int r = rowof ? rowof[i] : i;
-  if (r < 0 || r >= rpad) return;  // a slot whose expert id was out of range has no row
-  const size_t src = (size_t)(i / x_div) * ldx;
+  const int i0 = blockIdx.x * per;
+  const size_t src = (size_t)(i0 / x_div) * ldx;
   const float4* xr = (const float4*)(X + src);
   const float4* ur = up ? (const float4*)(up + src) : nullptr;
   __shared__ float red[8];
@@ -1240,8 +1240,6 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* u
     ex = 0;
   }
   const float sc = ldexpf(1.f, ex);
-  __half* hi = xg + (size_t)r * K;
-  __half* lo = xg + ((size_t)rpad + r) * K;
   for (int k = threadIdx.x; k < K / 4; k += 256) {
     const float4 v = srow[k];
     const float f[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
@@ -1253,10 +1251,19 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* u
     }
     const __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
     const __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
-    *(uint2*)(hi + 4 * k) = make_uint2(*(const uint32_t*)&h01, *(const uint32_t*)&h23);
-    *(uint2*)(lo + 4 * k) = make_uint2(*(const uint32_t*)&l01, *(const uint32_t*)&l23);
+    const uint2 hv = make_uint2(*(const uint32_t*)&h01, *(const uint32_t*)&h23);
+    const uint2 lv = make_uint2(*(const uint32_t*)&l01, *(const uint32_t*)&l23);
+    for (int q = 0; q < per; q++) {
+      const int r = rowof ? rowof[i0 + q] : i0 + q;
+      if (r < 0 || r >= rpad) continue;  // a slot whose expert id was out of range has no row
+      *(uint2*)(xg + (size_t)r * K + 4 * k) = hv;
+      *(uint2*)(xg + ((size_t)rpad + r) * K + 4 * k) = lv;
+    }
   }
-  if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
+  if (threadIdx.x < per) {
+    const int r = rowof ? rowof[i0 + threadIdx.x] : i0 + threadIdx.x;
+    if (r >= 0 && r < rpad) inv[r] = ldexpf(1.f, -ex);
+  }
 }
 
 // RMSNorm fused with the dense operand split (rows of DIM): the normalised
@@ -1662,7 +1669,7 @@ size_t tc_scratch_rows(int n) { return (size_t)n * N_USED + (size_t)N_EXPERT * 1
 cudaError_t tc_split(const float* X, int ldx, int K, int n, const TcScratch& sc, cudaStream_t s, const float* up) {
   const int rpad = dense_rpad(n);
   if (n <= 0 || K % 64 || K > TC_SPLIT_KMAX || ldx % 4 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
-  k_tc_split<<<n, 256, K * 4, s>>>(X, up, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv);
+  k_tc_split<<<n, 256, K * 4, s>>>(X, up, ldx, K, 1, nullptr, rpad, sc.xg, sc.inv, 1);
   return cudaGetLastError();
 }
 
@@ -1730,7 +1737,9 @@ cudaError_t tc_split_grouped(const float* X, int K, int x_div, int n, const TcSc
                              const float* up) {
   const int rpad = grouped_rpad(n);
   if (n <= 0 || K % 64 || K > TC_SPLIT_KMAX || x_div <= 0 || !fits(sc, rpad, K)) return cudaErrorInvalidValue;
-  k_tc_split<<<n * N_USED, 256, K * 4, s>>>(X, up, K, K, x_div, sc.rowof, rpad, sc.xg, sc.inv);
+  // one CTA per source row: the N_USED slots of a token share it when x_div == N_USED
+  const int per = x_div == N_USED ? N_USED : 1;
+  k_tc_split<<<n * N_USED / per, 256, K * 4, s>>>(X, up, K, K, x_div, sc.rowof, rpad, sc.xg, sc.inv, per);
   return cudaGetLastError();
 }
 
