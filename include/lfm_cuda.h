@@ -356,7 +356,10 @@ lfm_status lfm_q6k_prompt_gemm(const void* w_dev, uint32_t in_dim, uint32_t rows
  * e = expert_ids[t*4 + r] and slot q = t*4 + r,
  * y[q*rows + o] = sum_k W[e][o,k] x[(q / x_div)*in_dim + k]; x_div is 4 (one
  * activation row per token, the gate/up input) or 1 (one per slot, the down
- * input). n_expert == 32, rows % 128 == 0. Synchronous. */
+ * input). n_expert == 32, rows % 128 == 0. The four ids of a token must be
+ * distinct, as the router's top 4 are (LFM_ERR_ARG otherwise; ids outside
+ * 0..31 select no expert and leave their slot's rows unwritten).
+ * Synchronous. */
 lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t rows, uint32_t n_expert,
                                   const int32_t* expert_ids_dev, const float* x_dev, uint32_t x_div,
                                   uint32_t n, float* y_dev, void* stream);

@@ -152,7 +152,11 @@ void conv_batch(const float* bcx, const float* conv_w, float* state, size_t sstr
 void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s);
 // Router logits [n][32] of normalised tokens (f32_matmul, kernels.rs:552-574).
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s);
-void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s);
+// Per-expert slot lists: groups[e*(cap+1)] = count, then the slots routed to
+// e in slot order. A list longer than cap (a token naming one expert twice)
+// is cut at cap and raises GROUP_OVERFLOW in *overflow when given.
+constexpr unsigned GROUP_OVERFLOW = 4u;
+void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s, unsigned* overflow = nullptr);
 void swiglu_n(const float* gate, const float* up, size_t count, float* out, cudaStream_t s);
 void combine_n(const float* down, const float* selw, int n, float* x, cudaStream_t s);
 void add_n(float* x, const float* y, size_t count, cudaStream_t s);

@@ -198,6 +198,10 @@ struct CallScratch {
       if (e == cudaSuccess) e = cudaStreamSynchronize(s);
       if (e == cudaSuccess && h) {
         if (mem) cudaFreeAsync(mem, s);
+        if (h == lfm::GROUP_OVERFLOW) {
+          t_err = std::string(who) + ": the four expert ids of a token must be distinct";
+          return LFM_ERR_ARG;
+        }
         t_err = std::string(who) + ": a bounded wait in the kernel timed out";
         return LFM_ERR_DEVICE;
       }
@@ -240,7 +244,7 @@ lfm_status lfm_q6k_prompt_grouped(const void* w_dev, uint32_t in_dim, uint32_t r
   if (e == cudaSuccess) e = cudaMallocAsync(&groups, sizeof(int) * (size_t)lfm::N_EXPERT * (n + 1), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
   if (e == cudaSuccess) {
-    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s);
+    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s, cs.sc.err);
     e = lfm::tc_group(groups, (int)n, (int)n, cs.sc, s);
   }
   if (e == cudaSuccess) e = lfm::tc_split_grouped(x_dev, (int)in_dim, (int)x_div, (int)n, cs.sc, s);
@@ -293,7 +297,7 @@ lfm_status lfm_q6k_prompt_grouped_x16(const void* w_dev, const void* w16_dev, ui
   if (e == cudaSuccess) e = cudaMallocAsync(&groups, sizeof(int) * (size_t)lfm::N_EXPERT * (n + 1), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(cs.sc.err, 0, sizeof(unsigned), s);
   if (e == cudaSuccess) {
-    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s);
+    lfm::expert_groups(expert_ids_dev, (int)n, groups, (int)n, s, cs.sc.err);
     e = lfm::tc_group(groups, (int)n, (int)n, cs.sc, s);
   }
   if (e == cudaSuccess) e = lfm::tc_split_grouped(x_dev, (int)in_dim, (int)x_div, (int)n, cs.sc, s);

@@ -169,24 +169,46 @@ __global__ void __launch_bounds__(256) k_rmsnorm_n(const float* x, const float* 
 // Short conv over n tokens (kernels/resident.rs:33-56: three taps over
 // [state0, state1, b*x], the state rolling by one token per step). The taps
 // of token j are b*x of tokens j-2, j-1 (or the incoming state) and j, so
-// tokens are independent: thread (token, channel), same operation order as
-// the serial form. The new state is written by k_conv_state afterwards.
-__global__ void k_conv_prefill(const float* bcx, const float* conv_w, const float* state, int n, float* gated) {
+// tokens are independent: thread (channel, run of CONV_RUN tokens) slides the
+// two older taps along its run, reading b, c and x of each token once (all
+// of the run's loads issued before the first product), with the same
+// operations per token as the serial form. The new state is written by
+// k_conv_state afterwards.
+constexpr int CONV_RUN = 8;
+__global__ void __launch_bounds__(256) k_conv_prefill(const float* __restrict__ bcx, const float* __restrict__ conv_w,
+                                                      const float* __restrict__ state, int n,
+                                                      float* __restrict__ gated) {
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-  const int j = blockIdx.y;
-  if (ch >= DIM || j >= n) return;
+  const int j0 = blockIdx.y * CONV_RUN;
+  if (ch >= DIM || j0 >= n) return;
   auto bx_of = [&](int t) {
     const float* r = bcx + (size_t)t * 3 * DIM;
     return r[ch] * r[2 * DIM + ch];
   };
-  const float s0 = j >= 2 ? bx_of(j - 2) : (j == 1 ? state[2 * ch + 1] : state[2 * ch]);
-  const float s1 = j >= 1 ? bx_of(j - 1) : state[2 * ch + 1];
-  const float bx = bx_of(j);
-  float conv = 0.f;
-  conv += s0 * conv_w[3 * ch];
-  conv += s1 * conv_w[3 * ch + 1];
-  conv += bx * conv_w[3 * ch + 2];
-  gated[(size_t)j * DIM + ch] = bcx[(size_t)j * 3 * DIM + DIM + ch] * conv;
+  float b[CONV_RUN], c[CONV_RUN], x[CONV_RUN];
+#pragma unroll
+  for (int i = 0; i < CONV_RUN; i++) {
+    const float* r = bcx + (size_t)min(j0 + i, n - 1) * 3 * DIM;
+    b[i] = r[ch];
+    c[i] = r[DIM + ch];
+    x[i] = r[2 * DIM + ch];
+  }
+  // taps of token j0 (j0 is a multiple of CONV_RUN: 0 or >= 2)
+  float s0 = j0 >= 2 ? bx_of(j0 - 2) : state[2 * ch];
+  float s1 = j0 >= 1 ? bx_of(j0 - 1) : state[2 * ch + 1];
+  const float w0 = conv_w[3 * ch], w1 = conv_w[3 * ch + 1], w2 = conv_w[3 * ch + 2];
+#pragma unroll
+  for (int i = 0; i < CONV_RUN; i++) {
+    if (j0 + i >= n) break;
+    const float bx = b[i] * x[i];
+    float conv = 0.f;
+    conv += s0 * w0;
+    conv += s1 * w1;
+    conv += bx * w2;
+    gated[(size_t)(j0 + i) * DIM + ch] = c[i] * conv;
+    s0 = s1;
+    s1 = bx;
+  }
 }
 
 // Conv state after n tokens: (b*x of tokens n-2, n-1), or (old state1, b*x of
@@ -478,65 +500,80 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(const float* x, int len, i
 }
 
 // Router logits for n normalised tokens (f32_matmul, kernels.rs:552-574),
-// then route_n picks the top 4. One block per 16 tokens: 128-wide K chunks of
-// the 32 router rows and the 16 token rows are staged in shared memory, and
-// thread (token pair t / 32, expert t % 32) accumulates its two dots in K order
-// (float4 reads: three shared loads per eight FMAs). The next chunk's global
-// loads are in flight while the current one is multiplied.
-__global__ void __launch_bounds__(256) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
-  constexpr int KC = 128, TOK = 16, WS = KC + 4;  // WS: 16-byte skew per row, conflict-free float4 reads
-  constexpr int NW = N_EXPERT * KC / 4 / 256, NX = TOK * KC / 4 / 256;  // float4 loads per thread and chunk
-  __shared__ __align__(16) float xs[TOK][KC];
-  __shared__ __align__(16) float ws[N_EXPERT][WS];
-  const int t = threadIdx.x, j0 = blockIdx.x * TOK;
-  const int tp = t >> 5, e = t & 31;
-  float4 wr[NW], xr[NX];
-  auto fetch = [&](int k0) {
+// then route_n picks the top 4. A block of 4 warps takes 32 tokens; lane
+// (p, h) of warp w computes experts p and p + 16 for tokens 8w + 4h .. +3,
+// each logit one fmaf chain in K order (eight chains per lane). 64-wide K
+// chunks of the 32 router rows and the 32 token rows are staged in shared
+// memory by cp.async, the next chunk in flight while this one is multiplied;
+// per K step a lane reads two router float4 (16 distinct rows a warp, two
+// wavefronts) and four token float4 (two distinct rows, one wavefront) for
+// 32 FMAs.
+constexpr int RL_KC = 64, RL_TOK = 32, RL_RS = RL_KC + 4;  // RL_RS: row stride, conflict-free float4 reads
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__global__ void __launch_bounds__(128) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
+  static_assert(N_EXPERT == 32 && DIM % RL_KC == 0, "router tiling");
+  __shared__ __align__(16) float ws[2][N_EXPERT][RL_RS];
+  __shared__ __align__(16) float xs[2][RL_TOK][RL_RS];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int j0 = blockIdx.x * RL_TOK;
+  const int p = lane & 15, h = lane >> 4;
+  const int tr = warp * 8 + h * 4;  // this lane's first token row in the block
+  // chunk c into buffer b: 512 float4 of router rows and 512 of token rows,
+  // four of each per thread
+  auto fetch = [&](int c, int b) {
+    const int k0 = c * RL_KC;
 #pragma unroll
-    for (int i = 0; i < NW; i++) {
-      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
-      wr[i] = __ldg((const float4*)(Wr + (size_t)r * DIM + k0) + c4);
+    for (int i = 0; i < 4; i++) {
+      const int f = t + 128 * i, r = f >> 4, c4 = f & 15;
+      cp_async16(&ws[b][r][4 * c4], Wr + (size_t)r * DIM + k0 + 4 * c4);
+      cp_async16(&xs[b][r][4 * c4], xn + (size_t)min(j0 + r, n - 1) * DIM + k0 + 4 * c4);
     }
-#pragma unroll
-    for (int i = 0; i < NX; i++) {
-      const int f = t + 256 * i, r = f / (KC / 4), c4 = f % (KC / 4);
-      xr[i] = *((const float4*)(xn + (size_t)min(j0 + r, n - 1) * DIM + k0) + c4);
-    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  fetch(0);
-  float acc0 = 0.f, acc1 = 0.f;
-  for (int k0 = 0; k0 < DIM; k0 += KC) {
+  float acc[4][2];
 #pragma unroll
-    for (int i = 0; i < NW; i++) {
-      const int f = t + 256 * i;
-      *(float4*)&ws[f / (KC / 4)][4 * (f % (KC / 4))] = wr[i];
-    }
-#pragma unroll
-    for (int i = 0; i < NX; i++) {
-      const int f = t + 256 * i;
-      *(float4*)&xs[f / (KC / 4)][4 * (f % (KC / 4))] = xr[i];
+  for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.f;
+  constexpr int NC = DIM / RL_KC;
+  fetch(0, 0);
+  for (int c = 0; c < NC; c++) {
+    const int b = c & 1;
+    if (c + 1 < NC) {
+      fetch(c + 1, b ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    if (k0 + KC < DIM) fetch(k0 + KC);
-#pragma unroll 8
-    for (int k4 = 0; k4 < KC / 4; k4++) {
-      const float4 w = *(const float4*)&ws[e][4 * k4];
-      const float4 x0 = *(const float4*)&xs[2 * tp][4 * k4];
-      const float4 x1 = *(const float4*)&xs[2 * tp + 1][4 * k4];
-      acc0 = fmaf(w.x, x0.x, acc0);
-      acc0 = fmaf(w.y, x0.y, acc0);
-      acc0 = fmaf(w.z, x0.z, acc0);
-      acc0 = fmaf(w.w, x0.w, acc0);
-      acc1 = fmaf(w.x, x1.x, acc1);
-      acc1 = fmaf(w.y, x1.y, acc1);
-      acc1 = fmaf(w.z, x1.z, acc1);
-      acc1 = fmaf(w.w, x1.w, acc1);
+#pragma unroll 4
+    for (int k4 = 0; k4 < RL_KC / 4; k4++) {
+      const float4 wa = *(const float4*)&ws[b][p][4 * k4];
+      const float4 wb = *(const float4*)&ws[b][p + 16][4 * k4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 xv = *(const float4*)&xs[b][tr + i][4 * k4];
+        acc[i][0] = fmaf(wa.x, xv.x, acc[i][0]);
+        acc[i][0] = fmaf(wa.y, xv.y, acc[i][0]);
+        acc[i][0] = fmaf(wa.z, xv.z, acc[i][0]);
+        acc[i][0] = fmaf(wa.w, xv.w, acc[i][0]);
+        acc[i][1] = fmaf(wb.x, xv.x, acc[i][1]);
+        acc[i][1] = fmaf(wb.y, xv.y, acc[i][1]);
+        acc[i][1] = fmaf(wb.z, xv.z, acc[i][1]);
+        acc[i][1] = fmaf(wb.w, xv.w, acc[i][1]);
+      }
     }
-    __syncthreads();
+    __syncthreads();  // buffer b is refilled by the fetch of chunk c + 2
   }
-  const int ja = j0 + 2 * tp;
-  if (ja < n) logits[(size_t)ja * N_EXPERT + e] = acc0;
-  if (ja + 1 < n) logits[(size_t)(ja + 1) * N_EXPERT + e] = acc1;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int j = j0 + tr + i;
+    if (j < n) {
+      logits[(size_t)j * N_EXPERT + p] = acc[i][0];
+      logits[(size_t)j * N_EXPERT + p + 16] = acc[i][1];
+    }
+  }
 }
 
 // Router logits for few tokens (batched decode): one block per token, x
@@ -566,32 +603,72 @@ __global__ void __launch_bounds__(256) k_router_logits_tok(const float* Wr, cons
 }
 
 // Stable per-expert slot lists (kernels/persistent.rs:58-76): block e scans
-// the slots (token*4 + rank) in order, 1024 at a time, and appends those
-// routed to e (ballot within warps, prefix over the block's warps).
-__global__ void __launch_bounds__(1024) k_expert_groups(const int* sel, int n, int* groups, int cap) {
-  __shared__ int wcount[32];
+// the slots (token*4 + rank) in order and appends those routed to e. Each
+// thread takes GROUP_SPT consecutive slots a pass (16384 slots, 4096 tokens,
+// per pass), and a block-wide exclusive scan of the threads' hit counts gives
+// each hit its place, so every list is in slot order. A list never grows past
+// `cap` entries: a hit beyond it (only possible when a token names one expert
+// twice) is dropped, the count stops at cap and `overflow` (if given) gets
+// GROUP_OVERFLOW.
+constexpr int GROUP_SPT = 16;
+__global__ void __launch_bounds__(1024) k_expert_groups(const int* sel, int n, int* groups, int cap,
+                                                        unsigned* overflow) {
+  __shared__ int wpre[32];
+  __shared__ int wtot;
   const int e = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   int* g = groups + (size_t)e * (cap + 1);
   int count = 0;
   const int total = n * N_USED;
-  for (int s0 = 0; s0 < total; s0 += 1024) {
-    const int s = s0 + t;
-    const bool hit = s < total && sel[s] == e;
-    const unsigned m = __ballot_sync(0xffffffffu, hit);
-    if (lane == 0) wcount[warp] = __popc(m);
-    __syncthreads();
-    int before = 0, all = 0;
-#pragma unroll 8
-    for (int w = 0; w < 32; w++) {
-      const int c = wcount[w];
-      before += w < warp ? c : 0;
-      all += c;
+  const bool vec = ((uintptr_t)sel & 15) == 0;
+  for (int s0 = 0; s0 < total; s0 += 1024 * GROUP_SPT) {
+    const int base = s0 + t * GROUP_SPT;
+    unsigned m = 0;  // bit i: slot base + i is routed to e
+    if (vec && base + GROUP_SPT <= total) {
+#pragma unroll
+      for (int q = 0; q < GROUP_SPT / 4; q++) {
+        const int4 v = *((const int4*)(sel + base) + q);
+        m |= (unsigned)(v.x == e) << (4 * q) | (unsigned)(v.y == e) << (4 * q + 1) |
+             (unsigned)(v.z == e) << (4 * q + 2) | (unsigned)(v.w == e) << (4 * q + 3);
+      }
+    } else {
+      for (int i = 0; i < GROUP_SPT; i++)
+        if (base + i < total && sel[base + i] == e) m |= 1u << i;
     }
-    if (hit) g[1 + count + before + __popc(m & ((1u << lane) - 1u))] = s;
-    count += all;
+    const int c = __popc(m);
+    int inc = c;  // inclusive scan over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) wpre[warp] = inc;
     __syncthreads();
+    if (warp == 0) {
+      const int own = wpre[lane];
+      int winc = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, winc, o);
+        if (lane >= o) winc += v;
+      }
+      wpre[lane] = winc - own;
+      if (lane == 31) wtot = winc;
+    }
+    __syncthreads();
+    int pos = count + wpre[warp] + inc - c;
+    while (m) {
+      const int i = __ffs(m) - 1;
+      m &= m - 1;
+      if (pos < cap) g[1 + pos] = base + i;
+      pos++;
+    }
+    count += wtot;
+    __syncthreads();  // wpre / wtot are rewritten by the next pass
   }
-  if (t == 0) g[0] = count;
+  if (t == 0) {
+    g[0] = min(count, cap);
+    if (count > cap && overflow) atomicOr(overflow, GROUP_OVERFLOW);
+  }
 }
 
 __global__ void k_swiglu_n(const float* gate, const float* up, size_t count, float* out) {
@@ -655,7 +732,7 @@ void rmsnorm_n(const float* x, const float* w, float eps, int n, float* out, cud
 }
 
 void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated, cudaStream_t s) {
-  k_conv_prefill<<<dim3(DIM / 256, n), 256, 0, s>>>(bcx, conv_w, state, n, gated);
+  k_conv_prefill<<<dim3(DIM / 256, (n + CONV_RUN - 1) / CONV_RUN), 256, 0, s>>>(bcx, conv_w, state, n, gated);
   k_conv_state<<<DIM / 256, 256, 0, s>>>(bcx, state, n);
 }
 
@@ -698,11 +775,11 @@ void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s) {
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
   static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
   if (n < 256) k_router_logits_tok<<<n, 256, 0, s>>>(Wr, xnorm, logits);  // few tokens: a block each
-  else k_router_logits_n<<<(n + 15) / 16, 256, 0, s>>>(Wr, xnorm, n, logits);
+  else k_router_logits_n<<<(n + RL_TOK - 1) / RL_TOK, 128, 0, s>>>(Wr, xnorm, n, logits);
 }
 
-void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s) {
-  k_expert_groups<<<N_EXPERT, 1024, 0, s>>>(sel, n, groups, cap);
+void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s, unsigned* overflow) {
+  k_expert_groups<<<N_EXPERT, 1024, 0, s>>>(sel, n, groups, cap, overflow);
 }
 
 void swiglu_n(const float* gate, const float* up, size_t count, float* out, cudaStream_t s) {

@@ -1267,38 +1267,46 @@ __global__ void __launch_bounds__(256) k_tc_split(const float* X, const float* u
 }
 
 // RMSNorm fused with the dense operand split (rows of DIM): the normalised
-// row x * (1 / sqrt(mean(x^2) + eps)) * w is written to `normed` (fp32, the
-// same operations and order as the standalone rmsnorm kernel) and split into
-// the hi/lo operand like k_tc_split.
-__global__ void __launch_bounds__(256) k_tc_split_norm(const float* X, const float* w, float eps, float* normed,
-                                                       int rpad, __half* xg, float* inv) {
-  __shared__ float srow[DIM];
-  __shared__ float red[8];
-  const int r = blockIdx.x;
+// row x * (1 / sqrt(mean(x^2) + eps)) * w is written to `normed` (fp32) and
+// split into the hi/lo operand like k_tc_split. Thread t holds elements
+// t + 256 i (i < 8) in registers from the first load to the last store; the
+// sum of squares runs over them in that order, then over the warps.
+__global__ void __launch_bounds__(256) k_tc_split_norm(const float* __restrict__ X, const float* __restrict__ w,
+                                                       float eps, float* __restrict__ normed, int rpad,
+                                                       __half* __restrict__ xg, float* __restrict__ inv) {
+  constexpr int PER = DIM / 256;
+  __shared__ float red[8], redm[8];
+  const int r = blockIdx.x, t = threadIdx.x;
   const float* xr = X + (size_t)r * DIM;
+  float v[PER], g[PER];
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    v[i] = xr[t + 256 * i];
+    g[i] = __ldg(w + t + 256 * i);
+  }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < DIM; i += 256) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+  for (int i = 0; i < PER; i++) ss = fmaf(v[i], v[i], ss);
   ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  if ((t & 31) == 0) red[t >> 5] = ss;
   __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < 8; i++) t += red[i];
-  const float rinv = 1.0f / sqrtf(t / (float)DIM + eps);
+  float tot = 0.f;
+  for (int i = 0; i < 8; i++) tot += red[i];
+  const float rinv = 1.0f / sqrtf(tot / (float)DIM + eps);
   float mx = 0.f;
-  for (int i = threadIdx.x; i < DIM; i += 256) {
-    const float v = xr[i] * rinv * w[i];
-    srow[i] = v;
-    normed[(size_t)r * DIM + i] = v;
-    mx = fmaxf(mx, fabsf(v));
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    v[i] = v[i] * rinv * g[i];
+    normed[(size_t)r * DIM + t + 256 * i] = v[i];
+    mx = fmaxf(mx, fabsf(v[i]));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  __syncthreads();  // red is reused
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  if ((t & 31) == 0) redm[t >> 5] = mx;
   __syncthreads();
-  mx = red[0];
+  mx = redm[0];
 #pragma unroll
-  for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+  for (int i = 1; i < 8; i++) mx = fmaxf(mx, redm[i]);
   int ex = 0;
   if (mx > 0.f && mx < 3.0e38f) {
     frexpf(mx, &ex);
@@ -1309,20 +1317,14 @@ __global__ void __launch_bounds__(256) k_tc_split_norm(const float* X, const flo
   const float sc = ldexpf(1.f, ex);
   __half* hi = xg + (size_t)r * DIM;
   __half* lo = xg + ((size_t)rpad + r) * DIM;
-  for (int k = threadIdx.x * 4; k < DIM; k += 1024) {
-    __half h[4], l[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const float f = srow[k + j] * sc;
-      h[j] = __float2half_rn(f);
-      l[j] = __float2half_rn(f - __half2float(h[j]));
-    }
-    const __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
-    const __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
-    *(uint2*)(hi + k) = make_uint2(*(const uint32_t*)&h01, *(const uint32_t*)&h23);
-    *(uint2*)(lo + k) = make_uint2(*(const uint32_t*)&l01, *(const uint32_t*)&l23);
+  for (int i = 0; i < PER; i++) {
+    const float f = v[i] * sc;
+    const __half h = __float2half_rn(f);
+    hi[t + 256 * i] = h;
+    lo[t + 256 * i] = __float2half_rn(f - __half2float(h));
   }
-  if (threadIdx.x == 0) inv[r] = ldexpf(1.f, -ex);
+  if (t == 0) inv[r] = ldexpf(1.f, -ex);
 }
 
 // Split-K partials -> output, the splits summed in order (deterministic):

@@ -140,6 +140,38 @@ def test_prompt_grouped_vs_f64(cuda_lib, oracle_mod, in_dim, rows, x_div, n):
     assert _rel(got, ref) < TOL_SYNTH, _rel(got, ref)
 
 
+def test_prompt_grouped_unaligned_ids_and_repeats(cuda_lib):
+    """The slot lists read the expert ids four at a time when the id array is
+    16-byte aligned and one at a time otherwise: both give the same result.
+    A token naming one expert twice would grow that expert's list past its
+    capacity: the list stops there and the call returns LFM_ERR_ARG."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(17)
+    in_dim, rows, n = 2048, 128, 300
+    raw, w = _q6(cuda_lib, rng, in_dim, 32 * rows)
+    ids = np.stack([rng.choice(32, 4, replace=False) for _ in range(n)]).astype(np.int32).reshape(-1)
+    x = torch.from_numpy(rng.normal(0, 1, size=(n, in_dim)).astype(np.float32)).cuda()
+    buf = torch.zeros(4 * n + 1, dtype=torch.int32, device="cuda")
+    buf[: 4 * n] = torch.from_numpy(ids).cuda()
+    ya = torch.zeros((4 * n, rows), device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, 32, _ptr(buf), _ptr(x), 4, n,
+                                                        _ptr(ya), None), "aligned ids")
+    buf[1:] = torch.from_numpy(ids).cuda()  # the same ids 4 bytes further on
+    yb = torch.zeros((4 * n, rows), device="cuda")
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, 32,
+                                                        ctypes.c_void_p(buf.data_ptr() + 4), _ptr(x), 4, n,
+                                                        _ptr(yb), None), "unaligned ids")
+    assert torch.equal(ya, yb)
+    same = torch.full((4 * n,), 5, dtype=torch.int32, device="cuda")
+    st = cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, 32, _ptr(same), _ptr(x), 4, n, _ptr(ya), None)
+    assert st == 1  # LFM_ERR_ARG
+    assert b"distinct" in cuda_lib.lfm_ops_error()
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, 32, _ptr(buf), _ptr(x), 4, n,
+                                                        _ptr(yb), None), "after the rejected call")
+
+
 def test_prompt_gemm_rejects_bad_shapes(cuda_lib):
     import torch
     w = torch.zeros(100 * 8 * 210, dtype=torch.uint8, device="cuda")
