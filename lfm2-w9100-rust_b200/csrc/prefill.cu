@@ -504,56 +504,64 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(const float* x, int len, i
 // (p, h) of warp w computes experts p and p + 16 for tokens 8w + 4h .. +3,
 // each logit one fmaf chain in K order (eight chains per lane). 64-wide K
 // chunks of the 32 router rows and the 32 token rows are staged in shared
-// memory by cp.async, the next chunk in flight while this one is multiplied;
-// per K step a lane reads two router float4 (16 distinct rows a warp, two
-// wavefronts) and four token float4 (two distinct rows, one wavefront) for
-// 32 FMAs.
+// memory by cp.async through a ring of RL_STAGES buffers (a chunk's
+// multiply, ~700 cycles, is shorter than a load's latency, so three chunks
+// are in flight); per K step a lane reads two router float4 (16 distinct rows
+// a warp, two wavefronts) and four token float4 (two distinct rows, one
+// wavefront) for 32 FMAs.
 constexpr int RL_KC = 64, RL_TOK = 32, RL_RS = RL_KC + 4;  // RL_RS: row stride, conflict-free float4 reads
+constexpr int RL_STAGES = 4;
+constexpr int RL_STAGE_FLOATS = (N_EXPERT + RL_TOK) * RL_RS;
+constexpr int RL_SMEM = RL_STAGES * RL_STAGE_FLOATS * 4;  // 69632 bytes
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
 }
 __global__ void __launch_bounds__(128) k_router_logits_n(const float* Wr, const float* xn, int n, float* logits) {
-  static_assert(N_EXPERT == 32 && DIM % RL_KC == 0, "router tiling");
-  __shared__ __align__(16) float ws[2][N_EXPERT][RL_RS];
-  __shared__ __align__(16) float xs[2][RL_TOK][RL_RS];
+  static_assert(N_EXPERT == 32 && DIM % RL_KC == 0 && DIM / RL_KC >= RL_STAGES, "router tiling");
+  extern __shared__ __align__(16) float rl_smem[];  // stage b: router rows [32][RL_RS], then token rows [32][RL_RS]
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int j0 = blockIdx.x * RL_TOK;
   const int p = lane & 15, h = lane >> 4;
   const int tr = warp * 8 + h * 4;  // this lane's first token row in the block
-  // chunk c into buffer b: 512 float4 of router rows and 512 of token rows,
-  // four of each per thread
-  auto fetch = [&](int c, int b) {
-    const int k0 = c * RL_KC;
+  constexpr int NC = DIM / RL_KC;
+  // chunk c into its stage: 512 float4 of router rows and 512 of token rows,
+  // four of each per thread; one commit group per chunk (empty past the end,
+  // so that the group count stays uniform)
+  auto fetch = [&](int c) {
+    if (c < NC) {
+      float* ws = rl_smem + (c % RL_STAGES) * RL_STAGE_FLOATS;
+      float* xs = ws + N_EXPERT * RL_RS;
+      const int k0 = c * RL_KC;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int f = t + 128 * i, r = f >> 4, c4 = f & 15;
-      cp_async16(&ws[b][r][4 * c4], Wr + (size_t)r * DIM + k0 + 4 * c4);
-      cp_async16(&xs[b][r][4 * c4], xn + (size_t)min(j0 + r, n - 1) * DIM + k0 + 4 * c4);
+      for (int i = 0; i < 4; i++) {
+        const int f = t + 128 * i, r = f >> 4, c4 = f & 15;
+        cp_async16(ws + r * RL_RS + 4 * c4, Wr + (size_t)r * DIM + k0 + 4 * c4);
+        cp_async16(xs + r * RL_RS + 4 * c4, xn + (size_t)min(j0 + r, n - 1) * DIM + k0 + 4 * c4);
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   float acc[4][2];
 #pragma unroll
   for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.f;
-  constexpr int NC = DIM / RL_KC;
-  fetch(0, 0);
+#pragma unroll
+  for (int c = 0; c < RL_STAGES - 1; c++) fetch(c);
   for (int c = 0; c < NC; c++) {
-    const int b = c & 1;
-    if (c + 1 < NC) {
-      fetch(c + 1, b ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
+    // the stage refilled here was read in iteration c - 1, before its
+    // closing barrier
+    fetch(c + RL_STAGES - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(RL_STAGES - 1) : "memory");  // chunk c has landed
     __syncthreads();
+    const float* ws = rl_smem + (c % RL_STAGES) * RL_STAGE_FLOATS;
+    const float* xs = ws + N_EXPERT * RL_RS;
 #pragma unroll 4
     for (int k4 = 0; k4 < RL_KC / 4; k4++) {
-      const float4 wa = *(const float4*)&ws[b][p][4 * k4];
-      const float4 wb = *(const float4*)&ws[b][p + 16][4 * k4];
+      const float4 wa = *(const float4*)&ws[p * RL_RS + 4 * k4];
+      const float4 wb = *(const float4*)&ws[(p + 16) * RL_RS + 4 * k4];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const float4 xv = *(const float4*)&xs[b][tr + i][4 * k4];
+        const float4 xv = *(const float4*)&xs[(tr + i) * RL_RS + 4 * k4];
         acc[i][0] = fmaf(wa.x, xv.x, acc[i][0]);
         acc[i][0] = fmaf(wa.y, xv.y, acc[i][0]);
         acc[i][0] = fmaf(wa.z, xv.z, acc[i][0]);
@@ -564,7 +572,7 @@ __global__ void __launch_bounds__(128) k_router_logits_n(const float* Wr, const 
         acc[i][1] = fmaf(wb.w, xv.w, acc[i][1]);
       }
     }
-    __syncthreads();  // buffer b is refilled by the fetch of chunk c + 2
+    __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 4; i++) {
@@ -576,29 +584,43 @@ __global__ void __launch_bounds__(128) k_router_logits_n(const float* Wr, const 
   }
 }
 
-// Router logits for few tokens (batched decode): one block per token, x
-// staged in shared memory, warp w computes experts w, w+8, w+16, w+24 with
-// lane-strided K and a warp reduction.
-__global__ void __launch_bounds__(256) k_router_logits_tok(const float* Wr, const float* xn, float* logits) {
-  __shared__ float4 xs[DIM / 4];
-  const int j = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float4* x = (const float4*)(xn + (size_t)j * DIM);
-  for (int i = threadIdx.x; i < DIM / 4; i += 256) xs[i] = x[i];
-  __syncthreads();
+// Router logits for few tokens (batched decode, short prompts): block
+// (group of RT_TOK tokens, group of 8 experts); the group's x rows are staged
+// in shared memory and warp w computes expert 8 * blockIdx.y + w for all of
+// them, each router row read once per block. Per (token, expert) the sum is
+// lane-strided over K (lane l takes float4 l, l + 32, ...) and closed by a
+// warp butterfly.
+constexpr int RT_TOK = 4;
+__global__ void __launch_bounds__(256) k_router_logits_tok(const float* Wr, const float* xn, int n, float* logits) {
+  __shared__ float4 xs[RT_TOK][DIM / 4];
+  const int j0 = blockIdx.x * RT_TOK, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.y * 8 + warp;
 #pragma unroll
-  for (int q = 0; q < N_EXPERT / 8; q++) {
-    const int e = warp + 8 * q;
-    const float4* w = (const float4*)(Wr + (size_t)e * DIM);
-    float a = 0.f;
-    for (int i = lane; i < DIM / 4; i += 32) {
-      const float4 v = w[i], xv = xs[i];
-      a = fmaf(v.x, xv.x, a);
-      a = fmaf(v.y, xv.y, a);
-      a = fmaf(v.z, xv.z, a);
-      a = fmaf(v.w, xv.w, a);
+  for (int i = 0; i < RT_TOK * DIM / 4 / 256; i++) {
+    const int f = threadIdx.x + 256 * i, t = f / (DIM / 4), c = f % (DIM / 4);
+    xs[t][c] = *((const float4*)(xn + (size_t)min(j0 + t, n - 1) * DIM) + c);
+  }
+  __syncthreads();
+  const float4* w = (const float4*)(Wr + (size_t)e * DIM);
+  float a[RT_TOK];
+#pragma unroll
+  for (int t = 0; t < RT_TOK; t++) a[t] = 0.f;
+#pragma unroll 4
+  for (int i = lane; i < DIM / 4; i += 32) {
+    const float4 v = __ldg(w + i);
+#pragma unroll
+    for (int t = 0; t < RT_TOK; t++) {
+      const float4 xv = xs[t][i];
+      a[t] = fmaf(v.x, xv.x, a[t]);
+      a[t] = fmaf(v.y, xv.y, a[t]);
+      a[t] = fmaf(v.z, xv.z, a[t]);
+      a[t] = fmaf(v.w, xv.w, a[t]);
     }
-    a = warp_sum(a);
-    if (lane == 0) logits[(size_t)j * N_EXPERT + e] = a;
+  }
+#pragma unroll
+  for (int t = 0; t < RT_TOK; t++) {
+    const float r = warp_sum(a[t]);
+    if (lane == 0 && j0 + t < n) logits[(size_t)(j0 + t) * N_EXPERT + e] = r;
   }
 }
 
@@ -774,8 +796,14 @@ void argmax_rows(const float* x, int n, int len, int* out, cudaStream_t s) {
 
 void router_logits_n(const float* Wr, const float* xnorm, int n, float* logits, cudaStream_t s) {
   static_assert(N_EXPERT == 32, "router tiling assumes 32 experts");
-  if (n < 256) k_router_logits_tok<<<n, 256, 0, s>>>(Wr, xnorm, logits);  // few tokens: a block each
-  else k_router_logits_n<<<(n + RL_TOK - 1) / RL_TOK, 128, 0, s>>>(Wr, xnorm, n, logits);
+  if (n < 256) k_router_logits_tok<<<dim3((n + RT_TOK - 1) / RT_TOK, N_EXPERT / 8), 256, 0, s>>>(Wr, xnorm, n, logits);
+  else {
+    static unsigned long long done = 0;
+    static std::mutex mu;
+    once_per_device(done, mu,
+                    [] { cudaFuncSetAttribute(k_router_logits_n, cudaFuncAttributeMaxDynamicSharedMemorySize, RL_SMEM); });
+    k_router_logits_n<<<(n + RL_TOK - 1) / RL_TOK, 128, RL_SMEM, s>>>(Wr, xnorm, n, logits);
+  }
 }
 
 void expert_groups(const int* sel, int n, int* groups, int cap, cudaStream_t s, unsigned* overflow) {
