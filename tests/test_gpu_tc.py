@@ -140,6 +140,33 @@ def test_prompt_grouped_vs_f64(cuda_lib, oracle_mod, in_dim, rows, x_div, n):
     assert _rel(got, ref) < TOL_SYNTH, _rel(got, ref)
 
 
+def test_prompt_grouped_slot_lists_over_several_passes(cuda_lib, oracle_mod):
+    """5000 tokens = 20000 (token, rank) slots: the per-expert slot lists are
+    built in two passes of 16384 slots, and every slot's row must still land
+    in its expert's list in slot order (checked through the GEMM result)."""
+    import torch
+
+    import lfm2_b200
+    rng = np.random.default_rng(5000)
+    in_dim, rows, n = 512, 128, 5000
+    raw, w = _q6(cuda_lib, rng, in_dim, 32 * rows)
+    ids = np.stack([rng.choice(32, 4, replace=False) for _ in range(n)]).astype(np.int32).reshape(-1)
+    x = rng.normal(0, 1, size=(n, in_dim)).astype(np.float32)
+    y = torch.full((4 * n, rows), float("nan"), device="cuda")
+    idd, xd = torch.from_numpy(ids).cuda(), torch.from_numpy(x).cuda()
+    lfm2_b200.ops_check(cuda_lib.lfm_q6k_prompt_grouped(_ptr(w), in_dim, rows, 32, _ptr(idd), _ptr(xd), 4, n,
+                                                        _ptr(y), None), "prompt_grouped")
+    got = y.cpu().numpy().astype(np.float64)
+    wf = oracle_mod.dequant_blocks(raw).reshape(32, rows, in_dim).astype(np.float64)
+    ref = np.empty_like(got)
+    x64 = x.astype(np.float64)
+    for e in range(32):
+        q = np.nonzero(ids == e)[0]
+        ref[q] = x64[q // 4] @ wf[e].T
+    assert np.isfinite(got).all()
+    assert _rel(got, ref) < TOL_SYNTH, _rel(got, ref)
+
+
 def test_prompt_grouped_unaligned_ids_and_repeats(cuda_lib):
     """The slot lists read the expert ids four at a time when the id array is
     16-byte aligned and one at a time otherwise: both give the same result.
