@@ -167,6 +167,10 @@ struct EngineImpl {
 
   cudaGraphExec_t graph = nullptr;
   cudaGraphExec_t loop_graph = nullptr;  // advance + decode step, token fed back on device
+  // the batched decode step (lfm_batch_decode) of one session count as a CUDA
+  // graph: captured at the second step with that count, replayed after
+  cudaGraphExec_t bgraph = nullptr;
+  int bgraph_n = 0, bgraph_nl = 0, beager_n = 0;
   uint32_t* loop_tokens = nullptr;       // device record of loop tokens
   uint32_t loop_cap = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -213,6 +217,7 @@ struct EngineImpl {
     return (T*)p;
   }
   void free_state() {
+    drop_bgraph();  // it holds the status word's address
     for (void* p : state_allocs) cudaFree(p);
     state_allocs.clear();
     state_ready = false;
@@ -229,9 +234,17 @@ struct EngineImpl {
     }
   }
   void free_prefill() {
+    drop_bgraph();  // it holds the prompt buffers' addresses
     for (void* p : prefill_allocs) cudaFree(p);
     prefill_allocs.clear();
     ncap = 0;
+  }
+  void drop_bgraph() {
+    if (bgraph) {
+      cudaGraphExecDestroy(bgraph);
+      bgraph = nullptr;
+    }
+    bgraph_n = bgraph_nl = beager_n = 0;
   }
 
   // ------------------------------------------------------------- loading
@@ -1239,6 +1252,7 @@ void EngineImpl::batch_create(uint32_t nsess) {
 }
 
 void EngineImpl::batch_free() {
+  drop_bgraph();  // it holds the session buffers' addresses
   for (void* p : batch.allocs) cudaFree(p);
   batch = BatchState();
 }
@@ -1339,30 +1353,65 @@ void EngineImpl::run_batch_decode(uint32_t count, const uint32_t* tokens, const 
     B.h_map[n + i] = (int)pos[i];
     B.h_map[2 * n + i] = (int)sess[i];
   }
+  // embedding .. row argmax: every launch reads the step's inputs from B.map
+  // and device buffers that stay in place, so the same launches serve every
+  // step with n sessions
+  auto body = [&](int& cnt) {
+    embed_n(embd, (const uint32_t*)B.map, n, px, s);
+    cnt++;
+    TokBatch tb;
+    tb.pos = B.map + n;
+    tb.sess = B.map + 2 * n;
+    tb.kc = B.kc;
+    tb.vc = B.vc;
+    tb.conv = B.conv;
+    tb.kv_stride = B.kv_stride;
+    tb.conv_stride = B.conv_stride;
+    tb.part = B.attn_part;
+    enqueue_layers(n, 0, &tb, cnt);
+    // final norm + tied lm_head for every token, then the row argmax
+    if (use_tc && n >= tc_min) {
+      CK(tc_split_norm(px, out_norm, eps, n, ph, tcs, s));
+      CK(tc_gemm_q6(embd, n, B.logits, (int)hp.vocab, false, tcs, s, x16(embd)));
+    } else {
+      rmsnorm_n(px, out_norm, eps, n, ph, s);
+      gemm_q6_ld(embd, ph, n, B.logits, (int)hp.vocab, false, s);
+    }
+    argmax_rows(B.logits, n, (int)hp.vocab, B.next, s);
+    cnt += 3;
+  };
   CK(cudaEventRecord(ev0, s));
+  // the step's inputs (pageable host memory: a copy outside any graph)
   CK(cudaMemcpyAsync(B.map, B.h_map.data(), (size_t)3 * n * 4, cudaMemcpyHostToDevice, s));
-  embed_n(embd, (const uint32_t*)B.map, n, px, s);
-  nl++;
-  TokBatch tb;
-  tb.pos = B.map + n;
-  tb.sess = B.map + 2 * n;
-  tb.kc = B.kc;
-  tb.vc = B.vc;
-  tb.conv = B.conv;
-  tb.kv_stride = B.kv_stride;
-  tb.conv_stride = B.conv_stride;
-  tb.part = B.attn_part;
-  enqueue_layers(n, 0, &tb, nl);
-  // final norm + tied lm_head for every token, then the row argmax
-  if (use_tc && n >= tc_min) {
-    CK(tc_split_norm(px, out_norm, eps, n, ph, tcs, s));
-    CK(tc_gemm_q6(embd, n, B.logits, (int)hp.vocab, false, tcs, s, x16(embd)));
+  if (bgraph && bgraph_n == n) {
+    CK(cudaGraphLaunch(bgraph, s));
+    nl = bgraph_nl;
+    ctr.graph_replays++;
+  } else if (use_graph && beager_n == n) {
+    // the second step with this session count: capture it (the first, eager
+    // step has made every one-time kernel attribute call)
+    drop_bgraph();
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      body(nl);
+    } catch (...) {
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CK(cudaStreamEndCapture(s, &g));
+    const cudaError_t e = cudaGraphInstantiate(&bgraph, g, 0);
+    cudaGraphDestroy(g);
+    CK(e);
+    bgraph_n = n;
+    bgraph_nl = nl;
+    ctr.graph_captures++;
+    CK(cudaGraphLaunch(bgraph, s));
   } else {
-    rmsnorm_n(px, out_norm, eps, n, ph, s);
-    gemm_q6_ld(embd, ph, n, B.logits, (int)hp.vocab, false, s);
+    body(nl);
+    beager_n = n;
   }
-  argmax_rows(B.logits, n, (int)hp.vocab, B.next, s);
-  nl += 3;
   CK(cudaMemcpyAsync(next, B.next, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(h_io + 4, io + 4, 4, cudaMemcpyDeviceToHost, s));
   CK(cudaEventRecord(ev1, s));
