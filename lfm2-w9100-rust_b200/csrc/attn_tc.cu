@@ -67,6 +67,7 @@ struct AttnParams {
   float* out;      // out + j * out_stride + h * 64
   int out_stride;
   int start, n, ctx;
+  const int* start_dev;  // when set, the first position is read here (a replayed graph's launches keep their arguments)
   unsigned* err;
 };
 
@@ -109,7 +110,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
   const int qb = nqb - 1 - (int)blockIdx.y;  // longest rows first
   const int j0 = qb * AQ;
   const int last_tok = min(j0 + AQ, p.n) - 1;
-  const int ntiles = (p.start + last_tok) / KT + 1;
+  const int start = p.start_dev ? *p.start_dev : p.start;
+  const int ntiles = (start + last_tok) / KT + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, NSOFT);
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     const int h = kh * 4 + quarter;
     const int j = j0 + lane;
     const bool valid = j < p.n;
-    const int pr = p.start + j;  // last key position of this row
+    const int pr = start + j;  // last key position of this row
     {
       const float* qr = p.q + (size_t)(valid ? j : 0) * p.q_stride + h * HEAD_DIM;
 #pragma unroll
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 }  // namespace
 
 cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, const __half* vc, int start, int n,
-                            int ctx, float* out, int out_stride, unsigned* err, cudaStream_t s) {
+                            int ctx, float* out, int out_stride, unsigned* err, cudaStream_t s, const int* start_dev) {
   if (n <= 0 || start < 0 || start + n > ctx || q_stride % 4 || out_stride % 4 || ((uintptr_t)q & 15) ||
       ((uintptr_t)out & 15))
     return cudaErrorInvalidValue;
@@ -353,6 +355,7 @@ cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, cons
   p.out = out;
   p.out_stride = out_stride;
   p.start = start;
+  p.start_dev = start_dev;
   p.n = n;
   p.ctx = ctx;
   p.err = err;

@@ -171,6 +171,17 @@ struct EngineImpl {
   // graph: captured at the second step with that count, replayed after
   cudaGraphExec_t bgraph = nullptr;
   int bgraph_n = 0, bgraph_nl = 0, beager_n = 0;
+  // a prompt chunk of n <= LFM_PREFILL_CHUNK tokens of the engine's own
+  // session as a CUDA graph per n (its first position is read from io[1]):
+  // captured at the second chunk with that n, replayed after
+  struct PGraph {
+    int n = 0, nl = 0;
+    cudaGraphExec_t exec = nullptr;
+  };
+  static constexpr int PGRAPH_MAX = 8;
+  std::vector<PGraph> pgraphs;   // at most PGRAPH_MAX, oldest first
+  std::vector<int> pgraph_seen;  // chunk lengths run once eagerly
+  bool session_swap = false;     // kc / vc / conv_state point into a session slot
   uint32_t* loop_tokens = nullptr;       // device record of loop tokens
   uint32_t loop_cap = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -217,7 +228,8 @@ struct EngineImpl {
     return (T*)p;
   }
   void free_state() {
-    drop_bgraph();  // it holds the status word's address
+    drop_bgraph();  // both hold the status word's and the session state's addresses
+    drop_pgraphs();
     for (void* p : state_allocs) cudaFree(p);
     state_allocs.clear();
     state_ready = false;
@@ -234,7 +246,8 @@ struct EngineImpl {
     }
   }
   void free_prefill() {
-    drop_bgraph();  // it holds the prompt buffers' addresses
+    drop_bgraph();  // both hold the prompt buffers' addresses
+    drop_pgraphs();
     for (void* p : prefill_allocs) cudaFree(p);
     prefill_allocs.clear();
     ncap = 0;
@@ -245,6 +258,11 @@ struct EngineImpl {
       bgraph = nullptr;
     }
     bgraph_n = bgraph_nl = beager_n = 0;
+  }
+  void drop_pgraphs() {
+    for (PGraph& g : pgraphs) cudaGraphExecDestroy(g.exec);
+    pgraphs.clear();
+    pgraph_seen.clear();
   }
 
   // ------------------------------------------------------------- loading
@@ -269,7 +287,8 @@ struct EngineImpl {
   void run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep_mode = false);
   void ep_moe(const LayerW& L, const float* rows, int n, float* xres);
   void ep_reserve(int send_slots, int recv_slots);
-  void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs = nullptr);
+  void enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs = nullptr,
+                      const int* start_dev = nullptr);
   void batch_prefill_many(const uint32_t* sess, const uint32_t* ids, const uint32_t* lens, int count,
                           uint32_t* next);
   BatchState batch;
@@ -943,7 +962,8 @@ void EngineImpl::run_loop(uint32_t steps, uint32_t* out_tokens) {
 // tb != nullptr: one token from each of n independent sessions (batched
 // decode): positions, sessions and per-session caches come from tb, and every
 // token runs every layer.
-void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs) {
+void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& nl, const SessRuns* runs,
+                                const int* start_dev) {
   cudaStream_t s = stream;
   const float eps = hp.eps;
   LaunchCfg c;
@@ -991,8 +1011,10 @@ void EngineImpl::enqueue_layers(int n, uint32_t start, const TokBatch* tb, int& 
           nl += 2;
         }
       } else {
-        qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kc + loff, vc + loff, s);
-        if (tc) CK(attn_prefill_tc(pqkv, ld, kc + loff, vc + loff, (int)start, n, (int)ctx, pa, DIM, tcs.err, s));
+        qk_prep_n(pqkv, L.q_norm, L.k_norm, rope, start, n, ctx, eps, kc + loff, vc + loff, s, start_dev);
+        if (tc)
+          CK(attn_prefill_tc(pqkv, ld, kc + loff, vc + loff, (int)start, n, (int)ctx, pa, DIM, tcs.err, s,
+                             start_dev));
         else attn_prefill(pqkv, kc + loff, vc + loff, start, n, ctx, pa, s);
       }
       if (tc) split(pa, DIM);
@@ -1193,26 +1215,80 @@ void EngineImpl::run_prefill(const uint32_t* ids, int n, uint32_t start, bool ep
   }
   ep_now = ep_mode;
   CK(cudaEventRecord(ev0, s));
+  // the chunk's ids and its first position (pinned h_io[1] -> io[1], read by
+  // the attention launches): copies outside any graph
   CK(cudaMemcpyAsync(pids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-  embed_n(embd, pids, n, px, s);
-  nl++;
+  h_io[1] = (int)start;
+  CK(cudaMemcpyAsync(io + 1, h_io + 1, 4, cudaMemcpyHostToDevice, s));
+  // embedding .. lm_head argmax: for a given n the same launches serve every
+  // start position of the engine's own session
+  auto body = [&](int& cnt) {
+    embed_n(embd, pids, n, px, s);
+    cnt++;
+    enqueue_layers(n, start, nullptr, cnt, nullptr, io + 1);
+    LaunchCfg c;
+    c.stream = s;
+    c.pdl = false;
+    c.sms = sms;
+    if (use_mvt)
+      mvt_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2,
+                 (unsigned*)(io + 4), c);
+    else
+      mv_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
+    cnt++;
+  };
+  // chunks of up to LFM_PREFILL_CHUNK tokens (the api_stream prompt chunks,
+  // short turns) replay a graph per n; longer prompts and other sessions'
+  // slots launch one by one
+  const bool graphable =
+      use_graph && use_tc && !ep_mode && !session_swap && n >= tc_min && n <= (int)LFM_PREFILL_CHUNK;
+  PGraph* hit = nullptr;
+  bool seen = false;
+  if (graphable) {
+    for (PGraph& g : pgraphs)
+      if (g.n == n) hit = &g;
+    for (int v : pgraph_seen) seen = seen || v == n;
+  }
   try {
-    enqueue_layers(n, start, nullptr, nl);
+    if (hit) {
+      CK(cudaGraphLaunch(hit->exec, s));
+      nl = hit->nl;
+      ctr.graph_replays++;
+    } else if (graphable && seen) {
+      // the second chunk of this length: capture it (the first, eager chunk
+      // has made every one-time kernel attribute call)
+      cudaGraph_t g = nullptr;
+      CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      try {
+        body(nl);
+      } catch (...) {
+        cudaStreamEndCapture(s, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      CK(cudaStreamEndCapture(s, &g));
+      PGraph pg;
+      pg.n = n;
+      pg.nl = nl;
+      const cudaError_t e = cudaGraphInstantiate(&pg.exec, g, 0);
+      cudaGraphDestroy(g);
+      CK(e);
+      if ((int)pgraphs.size() >= PGRAPH_MAX) {
+        cudaGraphExecDestroy(pgraphs.front().exec);
+        pgraphs.erase(pgraphs.begin());
+      }
+      pgraphs.push_back(pg);
+      ctr.graph_captures++;
+      CK(cudaGraphLaunch(pg.exec, s));
+    } else {
+      body(nl);
+      if (graphable && pgraph_seen.size() < 2 * LFM_PREFILL_CHUNK) pgraph_seen.push_back(n);
+    }
   } catch (...) {
     ep_now = false;
     throw;
   }
   ep_now = false;
-  LaunchCfg c;
-  c.stream = s;
-  c.pdl = false;
-  c.sms = sms;
-  if (use_mvt)
-    mvt_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2,
-               (unsigned*)(io + 4), c);
-  else
-    mv_lmhead(embd, XSrc{px + (size_t)(n - 1) * DIM, out_norm, eps}, logits, am_part, counters + 128, io + 2, c);
-  nl++;
   CK(cudaMemcpyAsync(h_io + 2, io + 2, 12, cudaMemcpyDeviceToHost, s));
   CK(cudaEventRecord(ev1, s));
   CK(cudaStreamSynchronize(s));
@@ -1268,13 +1344,16 @@ uint32_t EngineImpl::batch_prefill(uint32_t sess, const uint32_t* ids, int n, bo
   vc = B.vc + (size_t)sess * B.kv_stride;
   conv_state = B.conv + (size_t)sess * B.conv_stride;
   CK(cudaMemsetAsync(conv_state, 0, B.conv_stride * 4, stream));  // a fresh session (reset_session)
+  session_swap = true;
   try {
     run_prefill(ids, n, 0, ep_mode);
   } catch (...) {
     kc = k0, vc = v0, conv_state = c0;
+    session_swap = false;
     throw;
   }
   kc = k0, vc = v0, conv_state = c0;
+  session_swap = false;
   return (uint32_t)h_io[2];
 }
 

@@ -133,8 +133,10 @@ void embed_n(const Q6Mat& E, const uint32_t* ids, int n, float* x, cudaStream_t 
 void rmsnorm_n(const float* x, const float* w, float eps, int n, float* out, cudaStream_t s);
 void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, float* gated,
                   cudaStream_t s);
+// (with start_dev the first position is read from device memory; it must equal `start`)
 void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope,
-               int start, int n, int ctx, float eps, __half* kc, __half* vc, cudaStream_t s);
+               int start, int n, int ctx, float eps, __half* kc, __half* vc, cudaStream_t s,
+               const int* start_dev = nullptr);
 void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int start, int n, int ctx,
                   float* out, cudaStream_t s);
 // Batched decode of independent sessions: token j is at position tpos[j] of

@@ -232,11 +232,11 @@ __global__ void k_conv_state(const float* bcx, float* state, int n) {
 // tpos[j] of session tsess[j], whose caches start sstride elements apart.
 __global__ void k_qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope,
                             int start, int ctx, float eps, __half* kc, __half* vc, const int* tpos,
-                            const int* tsess, size_t sstride) {
+                            const int* tsess, size_t sstride, const int* start_dev) {
   const int j = blockIdx.x;
   const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);  // 0..47
   const int lane = threadIdx.x & 31;
-  const int pos = tpos ? tpos[j] : start + j;
+  const int pos = tpos ? tpos[j] : (start_dev ? *start_dev : start) + j;
   if (tsess) {
     kc += (size_t)tsess[j] * sstride;
     vc += (size_t)tsess[j] * sstride;
@@ -759,8 +759,9 @@ void conv_prefill(const float* bcx, const float* conv_w, float* state, int n, fl
 }
 
 void qk_prep_n(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int start, int n,
-               int ctx, float eps, __half* kc, __half* vc, cudaStream_t s) {
-  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, start, ctx, eps, kc, vc, nullptr, nullptr, 0);
+               int ctx, float eps, __half* kc, __half* vc, cudaStream_t s, const int* start_dev) {
+  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, start, ctx, eps, kc, vc, nullptr, nullptr, 0,
+                                         start_dev);
 }
 
 void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int start, int n, int ctx, float* out,
@@ -771,7 +772,8 @@ void attn_prefill(const float* qkv, const __half* kc, const __half* vc, int star
 void qk_prep_batch(float* qkv, const float* q_norm, const float* k_norm, const float2* rope, int n, int ctx,
                    float eps, __half* kc, __half* vc, const int* tpos, const int* tsess, size_t sstride,
                    cudaStream_t s) {
-  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, 0, ctx, eps, kc, vc, tpos, tsess, sstride);
+  k_qk_prep_n<<<dim3(n, 6), 256, 0, s>>>(qkv, q_norm, k_norm, rope, 0, ctx, eps, kc, vc, tpos, tsess, sstride,
+                                         nullptr);
 }
 
 size_t attn_batch_part_floats(int n, int ctx) {

@@ -23,9 +23,11 @@ cudaError_t tc_gemm_f16_bmn(const __half* A, const __half* B, int M, int K, floa
 // Causal GQA prompt attention on the tensor cores for tokens [0, n) at
 // positions start.. (q of token j, head h at q + j*q_stride + h*64; K/V cache
 // [8][ctx][64] fp16 already holding positions 0..start+n-1); output at
-// out + j*out_stride + h*64.
+// out + j*out_stride + h*64. With start_dev the kernel reads the first
+// position from device memory (it must equal `start`, which the host checks).
 cudaError_t attn_prefill_tc(const float* q, int q_stride, const __half* kc, const __half* vc, int start, int n,
-                            int ctx, float* out, int out_stride, unsigned* err, cudaStream_t s);
+                            int ctx, float* out, int out_stride, unsigned* err, cudaStream_t s,
+                            const int* start_dev = nullptr);
 
 // Scratch of the Q6_K prompt GEMMs (engine-owned device memory): the hi/lo
 // activation operand, per-row inverse scales, and the grouped tile table,
